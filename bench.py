@@ -1,0 +1,467 @@
+"""Benchmark of the attention hot path on B200 (the driver's contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one decode-attention pass of the serving loop over one layer of a
+config-5-shaped batch: 256 sequences, context lengths ~ U[1024, 4096] (seed 3 +
+rank), GQA 24/8, head_dim 128, fp16 paged KV (block 64, shuffled block tables),
+16 layers of KV cache resident in HBM (~43 GB per GPU; steps rotate layers, so
+every step reads a layer larger than L2). A step writes each sequence's new
+token into the cache (slot-write kernel) and runs paged decode attention (split
+KV + combine). Under torchrun every rank owns its own 256 sequences (sequence
+partitioning, no collective on the data path): weak scaling.
+
+Headline ``value``: algorithmic HBM GB/s of the whole job (K/V bytes once + Q/O +
+block-table entries, summed over ranks, / max-over-ranks device time).
+Extra measurements on the same JSON line: the causal prefill of config 2
+(B4 x S2048, TFLOP/s) and decode on the config-3 shape, each against the
+measured roofline in MEASURED_PEAKS.json; ``e2e`` through the public API with
+pinned host buffers; ``cpu_baseline`` = the CPU oracle on a bounded sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HQ, HKV, D, BS = 24, 8, 128, 64
+DECODE_SEQS, DECODE_LO, DECODE_HI, DECODE_SEED = 256, 1024, 4096, 3
+DECODE_LAYERS = 16
+C3_SEQS, C3_LO, C3_HI, C3_SEED = 64, 512, 4096, 2
+PF_B, PF_S, PF_SEED = 4, 2048, 1
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ----------------------------------------------------------------- workloads
+def ragged_lens(n, lo, hi, seed):
+    return np.random.default_rng(seed).integers(lo, hi + 1, size=n).astype(np.int32)
+
+
+def make_tables(lens, rng):
+    nblk = [(int(x) + BS - 1) // BS for x in lens]
+    total = sum(nblk)
+    perm = rng.permutation(total).astype(np.int32)
+    bt = np.full((len(lens), max(nblk) + 1), -1, np.int32)
+    p = 0
+    for b, n in enumerate(nblk):
+        bt[b, :n] = perm[p:p + n]
+        p += n
+    return bt, total
+
+
+def decode_bytes(lens):
+    """Algorithmic HBM bytes of one decode pass: every K and V byte once (fp16),
+    Q and O (fp16) and one int32 block-table entry per page."""
+    lens = np.asarray(lens, np.int64)
+    return float(lens.sum() * HKV * D * 4 + len(lens) * HQ * D * 4 +
+                 sum(math.ceil(int(n) / BS) for n in lens) * 4)
+
+
+# ------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons with NVML during the timed region."""
+
+    def __init__(self, index):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        names = {
+            "hw_slowdown": getattr(nv, "nvmlClocksThrottleReasonHwSlowdown", 0x8),
+            "sw_thermal_slowdown": getattr(nv, "nvmlClocksThrottleReasonSwThermalSlowdown", 0x20),
+            "hw_thermal_slowdown": getattr(nv, "nvmlClocksThrottleReasonHwThermalSlowdown", 0x40),
+            "sw_power_cap": getattr(nv, "nvmlClocksThrottleReasonSwPowerCap", 0x4),
+        }
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+                for n, bit in names.items():
+                    if r & bit:
+                        self.reasons.add(n)
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self):
+        med = float(np.median(self.samples)) if self.samples else None
+        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples)}
+
+
+# --------------------------------------------------------------- our arm
+class DecodeWorkload:
+    def __init__(self, torch, dev, n_seqs, lo, hi, seed, layers):
+        rng = np.random.default_rng(seed + 1000)
+        self.lens = ragged_lens(n_seqs, lo, hi, seed)
+        # the step's new token sits at position len-1 (already counted in lens)
+        bt, total = make_tables(self.lens, rng)
+        self.total_pages = total
+        self.torch = torch
+        self.layers = layers
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        self.k = torch.empty(layers, total, BS, HKV, D, dtype=torch.float16, device=dev)
+        self.v = torch.empty_like(self.k)
+        for l in range(layers):
+            self.k[l].normal_(generator=g)
+            self.v[l].normal_(generator=g)
+        self.bt = torch.from_numpy(bt).to(dev)
+        self.ctx = torch.from_numpy(self.lens).to(dev)
+        self.start = (self.ctx - 1).contiguous()
+        self.q = torch.randn(n_seqs, HQ, D, device=dev, generator=g).half()
+        self.kn = torch.randn(n_seqs, 1, HKV, D, device=dev, generator=g).half()
+        self.vn = torch.randn(n_seqs, 1, HKV, D, device=dev, generator=g).half()
+        self.max_ctx = int(self.lens.max())
+        self.bytes = decode_bytes(self.lens)
+        from fast_infer_b200.kernels.attention import paged_attention_workspace_bytes
+        need = paged_attention_workspace_bytes(n_seqs, HQ, HKV, self.max_ctx)
+        self.ws = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+
+    def attend(self, layer, q=None):
+        from fast_infer_b200.kernels.attention import paged_attention
+        return paged_attention(self.q if q is None else q, self.k[layer], self.v[layer], self.bt,
+                               BS, 0, context_lens=self.ctx, max_context_len=self.max_ctx,
+                               workspace=self.ws)
+
+    def write(self, layer, kn=None, vn=None):
+        from fast_infer_b200._lib import check, load, strides
+        torch = self.torch
+        kn = self.kn if kn is None else kn
+        vn = self.vn if vn is None else vn
+        kc, vc = self.k[layer], self.v[layer]
+        st = load().fi_kv_write(
+            kn.data_ptr(), vn.data_ptr(), kc.data_ptr(), vc.data_ptr(), self.bt.data_ptr(),
+            self.start.data_ptr(), 0, None, kn.shape[0], 1, HKV, D, kc.shape[0], BS,
+            self.bt.shape[1], strides(*kn.stride()), strides(*vn.stride()),
+            strides(*kc.stride()), strides(*vc.stride()), strides(*self.bt.stride()), None,
+            torch.cuda.current_stream().cuda_stream)
+        check(st, "fi_kv_write")
+
+
+def timed(torch, fn, steps, warmup, dist=None):
+    """Device time of `steps` calls of fn(i) (CUDA events on the current stream),
+    bracketed by barrier + synchronize; returns max-over-ranks milliseconds."""
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        fn(warmup + i)
+    e1.record()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist_mod
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=dev)
+        dist = dist_mod
+    from fast_infer_b200 import _lib
+    _lib.load()
+    peaks, peak_kind = load_peaks()
+
+    # ---- headline: decode step over config-5-shaped batch, one per rank
+    wl = DecodeWorkload(torch, dev, DECODE_SEQS, DECODE_LO, DECODE_HI, DECODE_SEED + rank,
+                        DECODE_LAYERS)
+
+    def step(i):
+        layer = i % DECODE_LAYERS
+        wl.write(layer)
+        wl.attend(layer)
+
+    with ClockSampler(local) as clk:
+        ms = timed(torch, step, args.steps, args.warmup, dist)
+    ms_step = ms / args.steps
+    total_bytes = wl.bytes * world
+    value = total_bytes / (ms_step * 1e-3) / 1e9
+
+    # dominant op alone (paged decode + combine), for the roofline
+    ms_k = timed(torch, lambda i: wl.attend(i % DECODE_LAYERS), args.steps, args.warmup, None)
+    kern_ms = ms_k / args.steps
+    achieved = wl.bytes / (kern_ms * 1e-3) / 1e9
+    hbm_peak = float(peaks["hbm_gbs"])
+
+    # ---- e2e through the public API with pinned host buffers
+    n = DECODE_SEQS
+    hq = torch.randn(n, HQ, D).half().pin_memory()
+    hk = torch.randn(n, 1, HKV, D).half().pin_memory()
+    hv = torch.randn(n, 1, HKV, D).half().pin_memory()
+    ho = torch.empty(n, HQ, D, dtype=torch.float16).pin_memory()
+    dq = torch.empty(n, HQ, D, dtype=torch.float16, device=dev)
+    dk = torch.empty(n, 1, HKV, D, dtype=torch.float16, device=dev)
+    dv = torch.empty_like(dk)
+
+    def e2e_step(i):
+        layer = i % DECODE_LAYERS
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        wl.write(layer, dk, dv)
+        o = wl.attend(layer, dq)
+        ho.copy_(o, non_blocking=True)
+
+    ms_e = timed(torch, e2e_step, args.steps, args.warmup, dist)
+    e2e_step_ms = ms_e / args.steps
+    h2d = (hq.numel() + hk.numel() + hv.numel()) * 2
+    d2h = ho.numel() * 2
+
+    # ---- prefill, config 2 (B4 x S2048, 24/8, seed 1); 4 rotating input sets > L2
+    from fast_infer_b200.kernels.attention import flash_attention
+    g = torch.Generator(device=dev)
+    g.manual_seed(PF_SEED)
+    sets = []
+    for _ in range(4):
+        q = torch.randn(PF_B, HQ, PF_S, D, device=dev, generator=g).half()
+        k = torch.randn(PF_B, HKV, PF_S, D, device=dev, generator=g).half()
+        v = torch.randn(PF_B, HKV, PF_S, D, device=dev, generator=g).half()
+        sets.append((q, k, v, torch.empty_like(q)))
+    pf_steps = max(args.steps // 4, 10)
+    from fast_infer_b200._lib import check, load, strides
+    lib = load()
+
+    def pf(i):
+        q, k, v, o = sets[i % 4]
+        st = lib.fi_prefill_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), PF_B,
+                                HQ, HKV, PF_S, D, strides(*q.stride()), strides(*k.stride()),
+                                strides(*v.stride()), strides(*o.stride()), D ** -0.5, None,
+                                torch.cuda.current_stream().cuda_stream)
+        check(st, "fi_prefill_fwd")
+
+    ms_pf = timed(torch, pf, pf_steps, args.warmup, dist) / pf_steps
+    pf_flops = PF_B * HQ * 4.0 * D * PF_S * (PF_S + 1) / 2.0  # exact causal QK^T + PV
+    pf_tflops = pf_flops / (ms_pf * 1e-3) / 1e12
+    tc_peak = float(peaks["bf16_tflops"])
+
+    # ---- decode on the config-3 shape (64 seqs, ctx U[512,4096], seed 2)
+    wl3 = DecodeWorkload(torch, dev, C3_SEQS, C3_LO, C3_HI, C3_SEED + rank, 8)
+    ms3 = timed(torch, lambda i: wl3.attend(i % 8), args.steps, args.warmup, dist) / args.steps
+    c3_gbs = wl3.bytes / (ms3 * 1e-3) / 1e9
+
+    launches_per_step = 2 + (1 if _needs_combine(wl) else 0)
+    result = {
+        "metric": "decode-attn HBM GB/s",
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16 (fp32 softmax/accumulate)",
+        "data": "synthetic: N(0,1) fp16 K/V/Q, seeded ragged lengths and shuffled block tables",
+        "config": {
+            "workload": "config5-shaped ragged paged decode per rank: 256 seqs, ctx U[1024,4096] "
+                        "(seed 3+rank), GQA 24/8, D128, block 64, 16 resident layers rotated; "
+                        "step = KV slot write of the new token + paged decode",
+            "partition": "sequences (each rank owns 256 sequences x 8 KV heads)",
+            "l2": "inputs larger than L2 (one layer of KV = %.2f GB per step)" % (wl.bytes / 1e9),
+            "tokens_per_step": DECODE_SEQS * world,
+        },
+        "tokens_per_s": round(DECODE_SEQS * world / (ms_step * 1e-3), 1),
+        "roofline": {
+            "kernel": "paged_decode_kernel (+ split-KV combine)",
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
+            "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+            "peak_source": f"{peak_kind} hbm_gbs",
+            "traffic": None,
+        },
+        "prefill": {
+            "workload": "config 2: causal prefill B4 x S2048, GQA 24/8 (K/V not expanded), D128",
+            "ms": round(ms_pf, 4), "tflops": round(pf_tflops, 1),
+            "roofline": {"bound": "tensor", "achieved": round(pf_tflops, 1), "peak": tc_peak,
+                         "unit": "TFLOP/s", "frac": round(pf_tflops / tc_peak, 4),
+                         "peak_source": f"{peak_kind} bf16_tflops (burst)"},
+            "l2": "4 rotating input sets (536 MB) > L2",
+        },
+        "decode_config3": {
+            "workload": "config 3: 64 seqs, ctx U[512,4096] (seed 2), GQA 24/8",
+            "ms": round(ms3, 4), "gbs": round(c3_gbs, 1),
+            "frac": round(c3_gbs / hbm_peak, 4),
+        },
+        "e2e": {
+            "value": round(total_bytes / (e2e_step_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+            "ms_per_step": round(e2e_step_ms, 5),
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "path": "public API: H2D of q + new k/v from pinned memory, KV slot write, "
+                    "paged_attention(), D2H of the output",
+        },
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline_decode(wl.lens, threads=1)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result))
+
+
+def _needs_combine(wl):
+    from fast_infer_b200.kernels.attention import paged_attention_workspace_bytes
+    return paged_attention_workspace_bytes(DECODE_SEQS, HQ, HKV, wl.max_ctx) > 0
+
+
+# --------------------------------------------------------- CPU baselines
+def _cpu_decode_chunk(args):
+    seed, idx, lens = args
+    from oracle.attention_oracle import paged_attention_vectorized
+    rng = np.random.default_rng(seed)
+    sub = np.asarray(lens)[idx]
+    bt, total = make_tables(sub, rng)
+    kc = rng.standard_normal((total, BS, HKV, D), dtype=np.float32).astype(np.float16)
+    vc = rng.standard_normal((total, BS, HKV, D), dtype=np.float32).astype(np.float16)
+    q = rng.standard_normal((len(sub), HQ, D), dtype=np.float32).astype(np.float16)
+    t0 = time.perf_counter()
+    paged_attention_vectorized(q, kc, vc, bt, BS, sub)
+    return time.perf_counter() - t0, decode_bytes(sub)
+
+
+def cpu_baseline_decode(lens, threads=1, budget_s=12.0):
+    """Time the CPU oracle (per-block online-softmax decode in numpy) on a bounded
+    sample of the workload's sequences; returns GB/s of algorithmic bytes."""
+    lens = np.asarray(lens)
+    n = len(lens)
+    # grow the sample until it costs ~budget_s of CPU time (cap: whole batch)
+    sample = 8
+    done_s, done_b, used = 0.0, 0.0, 0
+    if threads <= 1:
+        while used < n and done_s < budget_s:
+            idx = np.arange(used, min(n, used + sample))
+            s, b = _cpu_decode_chunk((used, idx, lens))
+            done_s += s
+            done_b += b
+            used += len(idx)
+            sample *= 2
+        secs = done_s
+    else:
+        import multiprocessing as mp
+        ctx = mp.get_context("spawn")
+        chunks = [(i, np.arange(i, min(n, i + 4)), lens) for i in range(0, n, 4)]
+        t0 = time.perf_counter()
+        with ctx.Pool(threads) as pool:
+            res = pool.map(_cpu_decode_chunk, chunks)
+        secs = time.perf_counter() - t0
+        done_b = sum(r[1] for r in res)
+        used = n
+    return {"value": round(done_b / secs / 1e9, 4), "unit": "GB/s", "cores": threads,
+            "kind": "port",
+            "sample": f"{used} of {n} sequences of the decode workload (one layer), numpy "
+                      f"oracle paged_attention_vectorized, {secs:.1f} s"}
+
+
+def run_reference(args):
+    """Reference arm: the reference's algorithm on the host cores (the CPU oracle
+    port; the reference itself is Triton and has no CPU path of its own outside
+    its interpreter, which is not available on the GPU box)."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    ncores = os.cpu_count() or 1
+    lens = ragged_lens(DECODE_SEQS, DECODE_LO, DECODE_HI, DECODE_SEED)
+    vals = []
+    sub = lens[: max(16, 4 * ncores)]
+    t0 = time.perf_counter()
+    for _ in range(max(1, min(args.steps, 3))):
+        cb = cpu_baseline_decode(sub, threads=ncores)
+        vals.append(cb["value"])
+    value = float(np.median(vals))
+    result = {
+        "metric": "decode-attn HBM GB/s", "value": round(value, 4), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round((time.perf_counter() - t0) * 1e3 / max(1, len(vals)), 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 (numpy)", "data": "synthetic", "impl": "reference",
+        "config": {"workload": "config5-shaped ragged paged decode (sample of sequences)"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": ncores,
+                         "kind": "port", "sample": cb["sample"]},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(result))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,31 @@
+// Host-side helpers shared by the C-ABI entry points: error reporting, tensor-map
+// encoding through the driver entry point, device properties.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "fast_infer_b200.h"
+
+namespace fi {
+
+// Record a message for fi_last_error() and return `code`.
+int fail(int code, const char* fmt, ...);
+// Clear the thread's last-error message.
+void clear_error();
+// Map a CUDA runtime error to FI_ERR_CUDA with a message naming `what`.
+int cuda_fail(cudaError_t e, const char* what);
+
+// cuTensorMapEncodeTiled, resolved once through cudaGetDriverEntryPoint.
+// Returns FI_OK or FI_ERR_CUDA / FI_ERR_ALIGNMENT with a message.
+int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, const void* base,
+                 const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                 CUtensorMapSwizzle swizzle, const char* what);
+
+// Multiprocessor count of the current device (cached per device).
+int sm_count();
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace fi

@@ -1,0 +1,139 @@
+/*
+ * fast_infer_b200 — C ABI of the B200 (sm_100a) attention hot path.
+ *
+ * Drop-in boundary for Fast_Infer's attention path. Every entry point takes raw
+ * device pointers, element strides (int64, in elements, one per tensor dimension,
+ * outermost first), shapes, a softmax scale and a CUDA stream (cudaStream_t passed
+ * as void*). Nothing here allocates, synchronises the stream or keeps global state:
+ * calls are asynchronous on `stream`, re-entrant, and every buffer belongs to the
+ * caller. Each call returns FI_OK or an FI_ERR_* code after validating its
+ * arguments on the host; fi_last_error() then gives a one-line message
+ * (thread-local).
+ *
+ * Device-side faults the host cannot see before launch (a block-table entry
+ * outside the page pool, a pipeline wait that ran out of time) are OR-ed into the
+ * optional `error_flag` word (device int32, caller-zeroed) as FI_DEVERR_* bits.
+ * Pages with an invalid block-table entry are skipped, never dereferenced.
+ *
+ * Supported: fp16 Q/K/V/O, head_dim 128, KV page (block) size 64, GQA with
+ * num_q_heads % num_kv_heads == 0 and num_q_heads / num_kv_heads <= 8 for decode.
+ */
+#ifndef FAST_INFER_B200_H
+#define FAST_INFER_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define FI_OK 0
+#define FI_ERR_INVALID_ARG 1 /* null pointer, bad shape, inconsistent sizes */
+#define FI_ERR_UNSUPPORTED 2 /* valid input outside what the kernels implement */
+#define FI_ERR_ALIGNMENT 3   /* pointer or stride not 16-byte aligned where required */
+#define FI_ERR_WORKSPACE 4   /* workspace missing or too small */
+#define FI_ERR_CUDA 5        /* a CUDA runtime / driver call failed */
+
+/* ---- device error bits (OR-ed into *error_flag) ------------------------ */
+#define FI_DEVERR_TIMEOUT 1    /* an mbarrier wait exceeded its time bound; output undefined */
+#define FI_DEVERR_BAD_BLOCK 2  /* block_table entry outside [0, num_blocks) for a live token */
+#define FI_DEVERR_CONTEXT_LEN 4 /* a context length beyond max_context_len or the block table;
+                                  that sequence was truncated */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int fi_version(void);
+
+/* Message describing the last non-FI_OK return on this thread ("" if none). */
+const char* fi_last_error(void);
+
+/*
+ * Causal prefill attention (FlashAttention forward), tcgen05 UMMA + TMEM.
+ *
+ * Replaces: kernels/attention.py:80-113 `flash_attention(q, k, v, sm_scale)` and
+ * its Triton kernel `_flash_attn_fwd` (kernels/attention.py:8-77).
+ *
+ * q, o : [batch, num_q_heads, seq_len, 128] fp16, strides q_strides / o_strides
+ *        (4 entries each; innermost stride must be 1, the others multiples of 8).
+ * k, v : [batch, num_kv_heads, seq_len, 128] fp16. num_kv_heads may equal
+ *        num_q_heads (K/V already expanded, as the reference caller passes them)
+ *        or divide it (GQA without expansion: query head h reads K/V head
+ *        h / (num_q_heads / num_kv_heads)).
+ * o[b,h,i,:] = softmax_j<=i(q[b,h,i,:].k[b,hk,j,:] * sm_scale) . v[b,hk,:,:].
+ */
+int fi_prefill_fwd(const void* q, const void* k, const void* v, void* o, int64_t batch,
+                   int64_t num_q_heads, int64_t num_kv_heads, int64_t seq_len, int64_t head_dim,
+                   const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                   const int64_t* o_strides, float sm_scale, int32_t* error_flag, void* stream);
+
+/*
+ * Bytes of split-KV workspace fi_paged_decode needs for these sizes
+ * (pages_per_split = 0 selects the library's automatic split size).
+ */
+size_t fi_paged_decode_workspace_size(int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
+                                      int64_t head_dim, int64_t max_context_len,
+                                      int64_t block_size, int64_t pages_per_split);
+
+/*
+ * Paged decode attention (one query token per sequence) with GQA and split-KV.
+ *
+ * Replaces: kernels/attention.py:191-233 `paged_attention(q, k_cache, v_cache,
+ * block_table, block_size, num_tokens, sm_scale)` and its Triton kernel
+ * `_paged_attention_kernel` (kernels/attention.py:116-188).
+ *
+ * q, o        : [batch, num_q_heads, 128] fp16 (q_strides / o_strides: 3 entries).
+ * k_cache,
+ * v_cache     : [num_blocks, block_size=64, num_kv_heads, 128] fp16 page pools
+ *               (kc_strides / vc_strides: 4 entries; the layout of one layer of
+ *               kv_cache.py:25-28).
+ * block_table : [batch, max_blocks_per_seq] int32 (bt_strides: 2 entries), logical
+ *               page -> physical page; -1 marks an unused slot (kv_cache.py:33-34).
+ * context_lens: optional [batch] int32 device array of per-sequence token counts.
+ *               NULL = every sequence has `num_tokens` tokens (the reference's
+ *               scalar). `max_context_len` is a host-side upper bound of the
+ *               lengths, used only to size the launch (ignored when NULL).
+ *               Sequences with 0 tokens produce zeros (kernels/attention.py:205-206).
+ * workspace   : caller-owned device buffer of at least
+ *               fi_paged_decode_workspace_size(...) bytes (may be NULL when that is 0).
+ * pages_per_split: KV pages per split-KV partition; 0 = automatic.
+ */
+int fi_paged_decode(const void* q, const void* k_cache, const void* v_cache, void* o,
+                    const int32_t* block_table, const int32_t* context_lens, int64_t num_tokens,
+                    int64_t max_context_len, int64_t batch, int64_t num_q_heads,
+                    int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
+                    int64_t block_size, int64_t max_blocks_per_seq, const int64_t* q_strides,
+                    const int64_t* kc_strides, const int64_t* vc_strides,
+                    const int64_t* o_strides, const int64_t* bt_strides, float sm_scale,
+                    int64_t pages_per_split, void* workspace, size_t workspace_bytes,
+                    int32_t* error_flag, void* stream);
+
+/*
+ * KV-cache slot write: copy new tokens' K and V rows into their pages.
+ *
+ * Replaces: the slot writes of model.py:162-183 (`_store_kv_prefill`), model.py:185-201
+ * (`_store_kv_decode`) and kv_cache.py:69-102 (`KVCache.store`, `store_batch`), which the
+ * reference performs as one torch copy (plus a host sync) per (layer, sequence, block).
+ *
+ * k, v     : [batch, num_new, num_kv_heads, head_dim] fp16 (k_strides / v_strides:
+ *            4 entries, innermost 1).
+ * Token t of sequence b is written to logical position p = start_pos[b] + t (or
+ * start_pos_scalar + t when start_pos is NULL), i.e. to page
+ * block_table[b, p / block_size], row p % block_size, for t < n_new[b] (or all
+ * num_new tokens when n_new is NULL). Bytes are copied unchanged (bit-exact).
+ * Pages must already be allocated; an entry outside [0, num_blocks) sets
+ * FI_DEVERR_BAD_BLOCK and that row is skipped.
+ */
+int fi_kv_write(const void* k, const void* v, void* k_cache, void* v_cache,
+                const int32_t* block_table, const int32_t* start_pos, int64_t start_pos_scalar,
+                const int32_t* n_new, int64_t batch, int64_t num_new, int64_t num_kv_heads,
+                int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                int64_t max_blocks_per_seq, const int64_t* k_strides, const int64_t* v_strides,
+                const int64_t* kc_strides, const int64_t* vc_strides, const int64_t* bt_strides,
+                int32_t* error_flag, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FAST_INFER_B200_H */

@@ -1,0 +1,76 @@
+"""Seeded inputs of the golden fixtures (shared by make_golden.py, the tests and smoke()).
+
+numpy's ``default_rng`` makes them bit-identical on every machine, so only the
+reference's outputs need to be stored.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from oracle.attention_oracle import randn_f16
+
+
+def c1_inputs():
+    """Config 1 inputs (shared with tests): returns dict of numpy arrays."""
+    rng = np.random.default_rng(0)
+    B, Hq, Hkv, S, D, steps, NB = 1, 24, 8, 128, 128, 16, 64
+    return dict(
+        q=randn_f16(rng, (B, Hq, S, D)),
+        k=randn_f16(rng, (B, Hkv, S, D)),
+        v=randn_f16(rng, (B, Hkv, S, D)),
+        dq=randn_f16(rng, (steps, B, Hq, D)),
+        dk=randn_f16(rng, (steps, B, Hkv, D)),
+        dv=randn_f16(rng, (steps, B, Hkv, D)),
+        block_table=rng.permutation(NB).astype(np.int32)[None, :],
+        num_blocks=np.int64(NB),
+    )
+
+
+def prefill_small_inputs(S: int):
+    rng = np.random.default_rng(100 + S)
+    B, Hq, Hkv, D = 2, 6, 2, 128
+    return (randn_f16(rng, (B, Hq, S, D)), randn_f16(rng, (B, Hkv, S, D)),
+            randn_f16(rng, (B, Hkv, S, D)))
+
+
+PREFILL_SMALL_S = (1, 77, 200)
+DECODE_RAGGED_LENS = (1, 63, 64, 65, 300, 0, 129)
+
+
+def decode_ragged_inputs():
+    rng = np.random.default_rng(7)
+    Hq, Hkv, D, bs = 24, 8, 128, 64
+    lens = np.array(DECODE_RAGGED_LENS, np.int32)
+    B = len(lens)
+    nblk = [(int(n) + bs - 1) // bs for n in lens]
+    NB = sum(nblk) + 3  # a few spare pages that nobody references
+    perm = rng.permutation(NB).astype(np.int32)
+    max_blocks = max(nblk) + 1
+    bt = np.full((B, max_blocks), -1, np.int32)
+    p = 0
+    for b in range(B):
+        bt[b, : nblk[b]] = perm[p: p + nblk[b]]
+        p += nblk[b]
+    return dict(
+        q=randn_f16(rng, (B, Hq, D)),
+        k_cache=randn_f16(rng, (NB, bs, Hkv, D)),
+        v_cache=randn_f16(rng, (NB, bs, Hkv, D)),
+        block_table=bt,
+        context_lens=lens,
+    )
+
+
+KV_WRITE = dict(layers=2, heads=2, head_dim=128, max_seq_len=512, block=64,
+                batch=2, prefill=100, decode_steps=30)
+
+
+def kv_write_inputs():
+    c = KV_WRITE
+    rng = np.random.default_rng(11)
+    L, B, S, H, D = c["layers"], c["batch"], c["prefill"], c["heads"], c["head_dim"]
+    T = c["decode_steps"]
+    return dict(
+        pk=randn_f16(rng, (L, B, S, H, D)), pv=randn_f16(rng, (L, B, S, H, D)),
+        dk=randn_f16(rng, (T, L, B, H, D)), dv=randn_f16(rng, (T, L, B, H, D)),
+    )

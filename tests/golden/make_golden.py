@@ -1,0 +1,146 @@
+"""Generate golden vectors by running the reference implementation itself.
+
+Run once in a container that has the reference checkout (it is read, never
+modified); the outputs are small ``.npz`` fixtures committed next to this script:
+
+    python tests/golden/make_golden.py --reference <path-to-Fast_Infer-checkout>
+
+The reference's Triton kernels run on CPU under ``TRITON_INTERPRET=1``; its
+KV-cache methods run unchanged on CPU tensors. Inputs come from numpy's seeded
+``default_rng`` so any machine regenerates them bit-identically (the tests do).
+
+Fixtures:
+* ``c1.npz``            config 1: causal prefill B1 x S128 (24/8 heads, D128,
+                        seed 0) then 16 decode steps over a 64-block pool whose
+                        block table is a seeded permutation.
+* ``prefill_small.npz`` causal prefill, GQA 6/2 heads, D128, B2, S in {1, 77, 200}.
+* ``decode_ragged.npz`` paged decode, 24/8 heads, ragged lengths incl. 0 and
+                        block-boundary cases, one reference call per sequence.
+* ``kv_write.npz``      block tables + pool digests after the reference model's
+                        own ``_store_kv_prefill`` / ``_store_kv_decode``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import hashlib
+import os
+import sys
+import tempfile
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE.parent.parent))
+
+from tests.golden.inputs import (  # noqa: E402
+    DECODE_RAGGED_LENS, KV_WRITE, PREFILL_SMALL_S, c1_inputs, decode_ragged_inputs,
+    kv_write_inputs, prefill_small_inputs)
+
+
+def _import_reference(ref_path: str):
+    os.environ["TRITON_INTERPRET"] = "1"
+    tmp = tempfile.mkdtemp(prefix="fi_ref_")
+    os.symlink(os.path.abspath(ref_path), os.path.join(tmp, "fast_infer"))
+    sys.path.insert(0, tmp)
+    import torch  # noqa: F401
+    from fast_infer.kernels import attention as ref_attn  # type: ignore
+    from fast_infer import kv_cache as ref_kv  # type: ignore
+    from fast_infer import model as ref_model  # type: ignore
+    return ref_attn, ref_kv, ref_model
+
+
+def digest(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True)
+    args = ap.parse_args()
+    ref_attn, ref_kv, ref_model = _import_reference(args.reference)
+    import torch
+    T = torch.from_numpy
+
+    # ---- config 1 -------------------------------------------------------
+    c1 = c1_inputs()
+    q, k, v = T(c1["q"]), T(c1["k"]), T(c1["v"])
+    G = q.shape[1] // k.shape[1]
+    o_pre = ref_attn.flash_attention(q, k.repeat_interleave(G, dim=1),
+                                     v.repeat_interleave(G, dim=1)).numpy()
+    cache = ref_kv.KVCache(1, 8, 128, 64 * 64, 64, torch.device("cpu"))
+    cache.block_table[0] = T(c1["block_table"][0])
+    cache.free_blocks = []
+    # prefill tokens 0..127 through the reference's own store_batch (BHSD -> SHD)
+    cache.store_batch(0, 0, 0, k[0].transpose(0, 1), v[0].transpose(0, 1))
+    o_dec = []
+    for t in range(c1["dq"].shape[0]):
+        pos = 128 + t
+        cache.store(0, pos // 64, pos % 64, T(c1["dk"][t][0]), T(c1["dv"][t][0]))
+        o = ref_attn.paged_attention(T(c1["dq"][t]), cache.k[0], cache.v[0],
+                                     cache.block_table, 64, pos + 1)
+        o_dec.append(o.numpy())
+    np.savez_compressed(HERE / "c1.npz", o_prefill=o_pre, o_decode=np.stack(o_dec),
+                        k_pool_sha=digest(cache.k[0].numpy()),
+                        v_pool_sha=digest(cache.v[0].numpy()))
+
+    # ---- small prefill (GQA, ragged S) ------------------------------------
+    outs = {}
+    for S in PREFILL_SMALL_S:
+        q, k, v = (T(a) for a in prefill_small_inputs(S))
+        G = q.shape[1] // k.shape[1]
+        outs[f"o_S{S}"] = ref_attn.flash_attention(
+            q, k.repeat_interleave(G, dim=1), v.repeat_interleave(G, dim=1)).numpy()
+    np.savez_compressed(HERE / "prefill_small.npz", **outs)
+
+    # ---- ragged decode: one reference call per sequence --------------------
+    d = decode_ragged_inputs()
+    outs = []
+    for b, n in enumerate(d["context_lens"]):
+        o = ref_attn.paged_attention(T(d["q"][b:b + 1]), T(d["k_cache"]), T(d["v_cache"]),
+                                     T(d["block_table"][b:b + 1]), 64, int(n))
+        outs.append(o.numpy()[0])
+    # the reference's scalar-num_tokens launch over the whole batch (num_tokens = 64)
+    bt_all = d["block_table"].copy()
+    o_batch64 = ref_attn.paged_attention(
+        T(d["q"][2:5]), T(d["k_cache"]), T(d["v_cache"]), T(bt_all[2:5]), 64, 64).numpy()
+    np.savez_compressed(HERE / "decode_ragged.npz", o=np.stack(outs), o_batch64=o_batch64)
+
+    # ---- KV slot writes through the reference model's methods ----------------
+    c = KV_WRITE
+    w = kv_write_inputs()
+
+    class Cfg:
+        block_size = c["block"]
+
+    class Stub:
+        pass
+
+    stub = Stub()
+    stub.config = Cfg()
+    stub.kv_cache = ref_kv.KVCache(c["layers"], c["heads"], c["head_dim"], c["max_seq_len"],
+                                   c["block"], torch.device("cpu"))
+    stub.kv_cache._grow_batch(c["batch"])
+    M = ref_model.LlamaForCausalLM
+    for layer in range(c["layers"]):
+        M._store_kv_prefill(stub, layer, T(w["pk"][layer]), T(w["pv"][layer]))
+    bt_after_prefill = stub.kv_cache.block_table.numpy().copy()
+    stub._token_count = c["prefill"]
+    for t in range(c["decode_steps"]):
+        stub._token_count += 1
+        for layer in range(c["layers"]):
+            M._store_kv_decode(stub, layer, T(w["dk"][t, layer]), T(w["dv"][t, layer]))
+    np.savez_compressed(
+        HERE / "kv_write.npz",
+        bt_after_prefill=bt_after_prefill,
+        bt_final=stub.kv_cache.block_table.numpy(),
+        num_tokens=np.int64(stub.kv_cache.num_tokens),
+        free_blocks=np.array(stub.kv_cache.free_blocks, np.int64),
+        k_sha=digest(stub.kv_cache.k.numpy()), v_sha=digest(stub.kv_cache.v.numpy()),
+    )
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

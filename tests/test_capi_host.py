@@ -1,0 +1,105 @@
+"""C-ABI library: it loads, exports every symbol declared in include/*.h, and its
+host-side argument validation answers before any device work (no GPU needed)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from fast_infer_b200 import _lib
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _declared_symbols():
+    names = set()
+    for h in (ROOT / "include").glob("*.h"):
+        text = h.read_text()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names.update(re.findall(r"\b(fi_[a-z0-9_]+)\s*\(", text))
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    declared = _declared_symbols()
+    assert declared, "no declarations found"
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert declared == set(_lib.SIGNATURES), "ctypes signatures out of sync with the header"
+    assert lib.fi_version() >= 100
+
+
+def _nul():
+    return ctypes.c_void_p(0)
+
+
+def test_prefill_rejects_bad_head_dim_and_groups():
+    lib = _lib.load()
+    s4 = _lib.strides(1, 1, 1, 1)
+    st = lib.fi_prefill_fwd(1, 1, 1, 1, 1, 24, 8, 16, 64, s4, s4, s4, s4, 0.1, None, None)
+    assert st == _lib.FI_ERR_UNSUPPORTED
+    assert b"head_dim" in lib.fi_last_error()
+    st = lib.fi_prefill_fwd(1, 1, 1, 1, 1, 24, 7, 16, 128, s4, s4, s4, s4, 0.1, None, None)
+    assert st == _lib.FI_ERR_INVALID_ARG
+    st = lib.fi_prefill_fwd(None, None, None, None, 1, 24, 8, 16, 128, s4, s4, s4, s4, 0.1,
+                            None, None)
+    assert st == _lib.FI_ERR_INVALID_ARG
+    # empty problems are a no-op
+    assert lib.fi_prefill_fwd(None, None, None, None, 0, 24, 8, 16, 128, s4, s4, s4, s4, 0.1,
+                              None, None) == _lib.FI_OK
+
+
+def test_decode_validation_and_workspace_size():
+    lib = _lib.load()
+    s3, s4, s2 = _lib.strides(1, 1, 1), _lib.strides(1, 1, 1, 1), _lib.strides(1, 1)
+    args = lambda **kw: dict(dict(num_tokens=10, max_ctx=0, batch=2, hq=24, hkv=8, d=128,
+                                  nb=4, bs=64, mb=4), **kw)
+
+    def call(a, ptr=1):
+        return lib.fi_paged_decode(ptr, ptr, ptr, ptr, ptr, None, a["num_tokens"], a["max_ctx"],
+                                   a["batch"], a["hq"], a["hkv"], a["d"], a["nb"], a["bs"],
+                                   a["mb"], s3, s4, s4, s3, s2, 0.1, 0, None, 0, None, None)
+    assert call(args(d=64)) == _lib.FI_ERR_UNSUPPORTED
+    assert call(args(bs=16)) == _lib.FI_ERR_UNSUPPORTED
+    assert call(args(hq=25)) == _lib.FI_ERR_INVALID_ARG
+    assert call(args(hq=72, hkv=8)) == _lib.FI_ERR_UNSUPPORTED  # group of 9
+    assert call(args(num_tokens=4 * 64 + 1)) == _lib.FI_ERR_INVALID_ARG
+    assert call(args(), ptr=None) == _lib.FI_ERR_INVALID_ARG
+    # workspace: none for a single split, proportional to splits otherwise
+    assert lib.fi_paged_decode_workspace_size(2, 24, 8, 128, 64, 64, 0) == 0
+    ws = lib.fi_paged_decode_workspace_size(2, 24, 8, 128, 4096, 64, 8)
+    assert ws == 2 * 24 * (64 // 8) * (128 * 4 + 8)
+    # too-small workspace is reported before launch
+    st = lib.fi_paged_decode(1, 1, 1, 1, 1, None, 4096, 0, 2, 24, 8, 128, 64, 64, 64,
+                             s3, s4, s4, s3, s2, 0.1, 8, None, 0, None, None)
+    assert st == _lib.FI_ERR_WORKSPACE
+
+
+def test_kv_write_validation():
+    lib = _lib.load()
+    s4, s2 = _lib.strides(1, 1, 1, 1), _lib.strides(1, 1)
+    st = lib.fi_kv_write(None, None, None, None, None, None, 0, None, 1, 1, 8, 128, 4, 64, 4,
+                         s4, s4, s4, s4, s2, None, None)
+    assert st == _lib.FI_ERR_INVALID_ARG
+    st = lib.fi_kv_write(1, 1, 1, 1, 1, None, 250, None, 1, 10, 8, 128, 4, 64, 4,
+                         s4, s4, s4, s4, s2, None, None)
+    assert st == _lib.FI_ERR_INVALID_ARG  # positions 250..259 need a 5th block
+    assert lib.fi_kv_write(None, None, None, None, None, None, 0, None, 0, 1, 8, 128, 4, 64, 4,
+                           s4, s4, s4, s4, s2, None, None) == _lib.FI_OK
+
+
+def test_python_wrappers_reject_cpu_tensors():
+    import torch
+    from fast_infer_b200.kernels.attention import flash_attention, paged_attention
+    q = torch.zeros(1, 2, 4, 128, dtype=torch.float16)
+    with pytest.raises(ValueError, match="CUDA"):
+        flash_attention(q, q, q)
+    with pytest.raises(ValueError, match="CUDA"):
+        paged_attention(q[:, :, 0], torch.zeros(2, 64, 2, 128, dtype=torch.float16),
+                        torch.zeros(2, 64, 2, 128, dtype=torch.float16),
+                        torch.zeros(1, 2, dtype=torch.int32), 64, 5)
+    # reference semantics without touching the device: num_tokens == 0 -> zeros
+    out = paged_attention(q[:, :, 0], None, None, None, 64, 0)
+    assert out.shape == (1, 2, 128) and not out.any()
