@@ -225,10 +225,11 @@ def run_ours(args):
 
     # ---- headline: decode step over config-5-shaped batch, one per rank
     wl = DecodeWorkload(torch, dev, DECODE_SEQS, DECODE_LO, DECODE_HI, DECODE_SEED + rank,
-                        DECODE_LAYERS)
+                        args.layers)
+    nl = args.layers
 
     def step(i):
-        layer = i % DECODE_LAYERS
+        layer = i % nl
         wl.write(layer)
         wl.attend(layer)
 
@@ -239,7 +240,7 @@ def run_ours(args):
     value = total_bytes / (ms_step * 1e-3) / 1e9
 
     # dominant op alone (paged decode + combine), for the roofline
-    ms_k = timed(torch, lambda i: wl.attend(i % DECODE_LAYERS), args.steps, args.warmup, None)
+    ms_k = timed(torch, lambda i: wl.attend(i % nl), args.steps, args.warmup, None)
     kern_ms = ms_k / args.steps
     achieved = wl.bytes / (kern_ms * 1e-3) / 1e9
     hbm_peak = float(peaks["hbm_gbs"])
@@ -255,7 +256,7 @@ def run_ours(args):
     dv = torch.empty_like(dk)
 
     def e2e_step(i):
-        layer = i % DECODE_LAYERS
+        layer = i % nl
         dq.copy_(hq, non_blocking=True)
         dk.copy_(hk, non_blocking=True)
         dv.copy_(hv, non_blocking=True)
@@ -270,27 +271,11 @@ def run_ours(args):
 
     # ---- prefill, config 2 (B4 x S2048, 24/8, seed 1); 4 rotating input sets > L2
     from fast_infer_b200.kernels.attention import flash_attention
-    g = torch.Generator(device=dev)
-    g.manual_seed(PF_SEED)
-    sets = []
-    for _ in range(4):
-        q = torch.randn(PF_B, HQ, PF_S, D, device=dev, generator=g).half()
-        k = torch.randn(PF_B, HKV, PF_S, D, device=dev, generator=g).half()
-        v = torch.randn(PF_B, HKV, PF_S, D, device=dev, generator=g).half()
-        sets.append((q, k, v, torch.empty_like(q)))
+    sets = prefill_inputs(torch, dev, 4)
     pf_steps = max(args.steps // 4, 10)
-    from fast_infer_b200._lib import check, load, strides
-    lib = load()
-
-    def pf(i):
-        q, k, v, o = sets[i % 4]
-        st = lib.fi_prefill_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), PF_B,
-                                HQ, HKV, PF_S, D, strides(*q.stride()), strides(*k.stride()),
-                                strides(*v.stride()), strides(*o.stride()), D ** -0.5, None,
-                                torch.cuda.current_stream().cuda_stream)
-        check(st, "fi_prefill_fwd")
-
-    ms_pf = timed(torch, pf, pf_steps, args.warmup, dist) / pf_steps
+    lib = _lib.load()
+    ms_pf = timed(torch, lambda i: prefill_call(torch, lib, sets[i % 4]), pf_steps, args.warmup,
+                  dist) / pf_steps
     pf_flops = PF_B * HQ * 4.0 * D * PF_S * (PF_S + 1) / 2.0  # exact causal QK^T + PV
     pf_tflops = pf_flops / (ms_pf * 1e-3) / 1e12
     tc_peak = float(peaks["bf16_tflops"])
@@ -360,6 +345,56 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(result))
+
+
+def prefill_inputs(torch, dev, nsets):
+    g = torch.Generator(device=dev)
+    g.manual_seed(PF_SEED)
+    sets = []
+    for _ in range(nsets):
+        q = torch.randn(PF_B, HQ, PF_S, D, device=dev, generator=g).half()
+        k = torch.randn(PF_B, HKV, PF_S, D, device=dev, generator=g).half()
+        v = torch.randn(PF_B, HKV, PF_S, D, device=dev, generator=g).half()
+        sets.append((q, k, v, torch.empty_like(q)))
+    return sets
+
+
+def prefill_call(torch, lib, qkvo):
+    from fast_infer_b200._lib import check, strides
+    q, k, v, o = qkvo
+    st = lib.fi_prefill_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), PF_B,
+                            HQ, HKV, PF_S, D, strides(*q.stride()), strides(*k.stride()),
+                            strides(*v.stride()), strides(*o.stride()), D ** -0.5, None,
+                            torch.cuda.current_stream().cuda_stream)
+    check(st, "fi_prefill_fwd")
+
+
+def run_only(args):
+    """One kernel family alone, for profiling (ncu) and quick sweeps."""
+    import torch
+    from fast_infer_b200._lib import load
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lib = load()
+    peaks, peak_kind = load_peaks()
+    out = {"only": args.only, "steps": args.steps, "warmup": args.warmup}
+    if args.only == "prefill":
+        sets = prefill_inputs(torch, dev, 4)
+        ms = timed(torch, lambda i: prefill_call(torch, lib, sets[i % 4]), args.steps,
+                   args.warmup) / args.steps
+        tf = PF_B * HQ * 4.0 * D * PF_S * (PF_S + 1) / 2.0 / (ms * 1e-3) / 1e12
+        out.update(ms=round(ms, 4), tflops=round(tf, 1),
+                   frac=round(tf / float(peaks["bf16_tflops"]), 4))
+    else:
+        c3 = args.only == "decode_c3"
+        wl = DecodeWorkload(torch, dev, C3_SEQS if c3 else DECODE_SEQS, C3_LO if c3 else DECODE_LO,
+                            C3_HI if c3 else DECODE_HI, C3_SEED if c3 else DECODE_SEED,
+                            args.layers)
+        ms = timed(torch, lambda i: wl.attend(i % args.layers), args.steps, args.warmup) / args.steps
+        gbs = wl.bytes / (ms * 1e-3) / 1e9
+        out.update(ms=round(ms, 4), gbs=round(gbs, 1), bytes=wl.bytes,
+                   frac=round(gbs / float(peaks["hbm_gbs"]), 4))
+    print(json.dumps(out))
 
 
 def _needs_combine(wl):
@@ -454,11 +489,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", choices=["decode", "decode_c3", "prefill"], default=None,
+                    help="time one kernel family alone (profiling runs); prints one JSON line")
+    ap.add_argument("--layers", type=int, default=DECODE_LAYERS,
+                    help="resident KV-cache layers of the decode workload")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.only:
+        run_only(args)
     else:
         run_ours(args)
 

@@ -1,0 +1,83 @@
+"""Multi-rank host logic on CPU (gloo, world_size 2): KV-head and sequence
+partitioning reproduce the unsharded attention exactly, and the head all-gather
+reassembles outputs in head order."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from fast_infer_b200.shard import head_shard, seq_range
+
+
+def test_head_shard_ranges():
+    shards = [head_shard(r, 4, 24, 8) for r in range(4)]
+    assert [(s.kv_start, s.kv_end) for s in shards] == [(0, 2), (2, 4), (4, 6), (6, 8)]
+    assert [(s.q_start, s.q_end) for s in shards] == [(0, 6), (6, 12), (12, 18), (18, 24)]
+    s8 = head_shard(7, 8, 24, 8)
+    assert (s8.kv_start, s8.q_start, s8.q_end) == (7, 21, 24)
+    with pytest.raises(ValueError):
+        head_shard(0, 3, 24, 8)
+    # every query head's KV head is on the same rank
+    for r in range(8):
+        s = head_shard(r, 8, 24, 8)
+        assert all(s.kv_start <= h // 3 < s.kv_end for h in range(s.q_start, s.q_end))
+
+
+def test_seq_range_covers_batch():
+    for world in (1, 2, 3, 8):
+        spans = [seq_range(r, world, 13) for r in range(world)]
+        assert spans[0][0] == 0 and spans[-1][1] == 13
+        assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q, k, v, result_q):
+    import torch.distributed as dist
+    from fast_infer_b200.shard import gather_heads, head_shard, shard_heads
+    from oracle.attention_oracle import attention_fp32
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        s = head_shard(rank, world, q.shape[1], k.shape[1])
+        ql = shard_heads(torch.from_numpy(q), s, kv=False).numpy()
+        kl = shard_heads(torch.from_numpy(k), s, kv=True).numpy()
+        vl = shard_heads(torch.from_numpy(v), s, kv=True).numpy()
+        ol = attention_fp32(ql, kl, vl)                       # [B, Hq_r, S, D]
+        B, Hr, S, D = ol.shape
+        flat = torch.from_numpy(ol).permute(0, 2, 1, 3).reshape(B, S, Hr * D)
+        full = gather_heads(flat)                             # [B, S, Hq*D]
+        if rank == 0:
+            result_q.put(full.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_kv_head_partition_allgather_matches_unsharded():
+    rng = np.random.default_rng(0)
+    B, Hq, Hkv, S, D = 2, 24, 8, 40, 128
+    q = rng.standard_normal((B, Hq, S, D), dtype=np.float32).astype(np.float16)
+    k = rng.standard_normal((B, Hkv, S, D), dtype=np.float32).astype(np.float16)
+    v = rng.standard_normal((B, Hkv, S, D), dtype=np.float32).astype(np.float16)
+    ctx = mp.get_context("spawn")
+    result_q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, k, v, result_q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    full = result_q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    from oracle.attention_oracle import attention_fp32
+    ref = attention_fp32(q, k, v).transpose(0, 2, 1, 3).reshape(B, S, Hq * D)
+    assert np.array_equal(full, ref)
