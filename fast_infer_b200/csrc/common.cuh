@@ -71,6 +71,33 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded busy-poll (test_wait never suspends the thread): lowest wake-up
+// latency, for waits on the critical path of a pipeline.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((++spins & 1023u) == 0u && globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      set_error(err, FI_DEVERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // Bounded wait for the phase with the given parity to complete. Returns false
 // (and records FI_DEVERR_TIMEOUT) if it did not complete within kWaitTimeoutNs.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
@@ -133,6 +160,35 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Warpgroup register reallocation (all warps of a warpgroup execute it).
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// Named-barrier sync of one warpgroup (128 threads) that also ANDs a predicate
+// across it (bar.red.and).
+__device__ __forceinline__ bool wg_bar_and(int id, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ void named_bar_arrive(int id, int nthreads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
@@ -171,6 +227,62 @@ __device__ __forceinline__ void mma_16816(float* c, uint32_t a0, uint32_t a1, ui
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Packed fp32x2 helpers (sm_100 FFMA2 / FADD2): two lanes of work per instruction.
+__device__ __forceinline__ uint64_t f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ void f32x2_split(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// 2^x for a pair of floats on the FMA/ALU pipes (no MUFU): x = n + f with
+// n = round(x) (magic-constant rounding) and f in [-0.5, 0.5]; 2^f from a degree-3
+// minimax polynomial (coefficients fitted here by a Remez exchange on relative
+// error, max relative error 7.5e-5), 2^n added to the exponent field as an
+// integer. Inputs are clamped to >= -126 so -inf maps to ~1e-38 (0 once rounded
+// to fp16); valid for x <= 127.
+__device__ __forceinline__ void exp2_poly_x2(uint64_t x2, float& r0, float& r1) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  float x0, x1;
+  f32x2_split(x2, x0, x1);
+  x0 = fmaxf(x0, -126.0f);
+  x1 = fmaxf(x1, -126.0f);
+  const uint64_t x = f32x2(x0, x1);
+  const uint64_t t = add_f32x2(x, f32x2(kMagic, kMagic));
+  const uint64_t n = add_f32x2(t, f32x2(-kMagic, -kMagic));
+  const uint64_t f = fma_f32x2(n, f32x2(-1.0f, -1.0f), x);
+  uint64_t q = fma_f32x2(f32x2(0.0551716685f, 0.0551716685f), f,
+                         f32x2(0.2426111251f, 0.2426111251f));
+  q = fma_f32x2(q, f, f32x2(0.6932609677f, 0.6932609677f));
+  q = fma_f32x2(q, f, f32x2(0.9999280572f, 0.9999280572f));
+  float q0, q1, t0, t1;
+  f32x2_split(q, q0, q1);
+  f32x2_split(t, t0, t1);
+  r0 = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23));
+  r1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23));
 }
 
 __device__ __forceinline__ float fast_exp2(float x) {

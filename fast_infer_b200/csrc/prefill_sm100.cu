@@ -39,20 +39,38 @@ constexpr int kBN = 128;            // keys per KV tile
 constexpr int kHD = 128;            // head dim
 constexpr int kHalfBytes = kBM * 128;      // 128 rows x 64 fp16 (one swizzle column)
 constexpr int kTileBytes = 2 * kHalfBytes; // 32 KB: a 128 x 128 fp16 tile
-constexpr int kPfThreads = 320;
+// 3 warpgroups: two softmax warpgroups (one per Q tile) and one for the TMA
+// producer (warp 8) and UMMA issuer (warp 9); warps 10-11 only hand their
+// registers to the softmax warpgroups (setmaxnreg).
+constexpr int kPfThreads = 384;
+constexpr int kRegsSoftmax = 184;  // 2 x 128 x 184 + 128 x 136 = 384 x 168
+constexpr int kRegsOther = 136;
+constexpr int kTeardownBar = 15;   // named barrier: all roles done, TMEM can be freed
 constexpr int kPfStages = 2;
 // Q0, Q1, K[2], V[2] tiles + barriers + tmem slot, plus 1 KB for alignment.
 constexpr int kPfSmemBytes = 1024 + (2 + 2 * kPfStages) * kTileBytes + 256;
 
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+// Of every 8 column pairs of S, this many take exp2 on the FMA pipe (polynomial)
+// instead of MUFU, so the two units share the softmax's exponentials.
+#ifndef FI_PF_EMU_PAIRS
+#define FI_PF_EMU_PAIRS 2
+#endif
+constexpr int kEmuPairsPer8 = FI_PF_EMU_PAIRS;
+#ifndef FI_PF_SPIN
+#define FI_PF_SPIN 0
+#endif
+// Critical-path waits (S ready, P ready) busy-poll instead of suspending.
+__device__ __forceinline__ bool crit_wait(uint64_t* bar, uint32_t parity, int* err) {
+#if FI_PF_SPIN
+  return mbar_wait_spin(bar, parity, err);
+#else
+  return mbar_wait(bar, parity, err);
+#endif
+}
 
-struct PrefillParams {
-  int batch, hq, hk, group, seq_len, npairs;
-  float scale_log2;
-  int* err;
-};
-
-// Shared-memory matrix descriptor, 128-byte swizzle (sm_100 "version 1" format).
+// Shared-memory matrix descriptor, 128-byte swizzle (sm_100 "version 1" format):
+// start address, leading / stride byte offsets (16-byte units), layout type 2.
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
@@ -63,26 +81,65 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo
   return d;
 }
 
-// Instruction descriptor: f16 x f16 -> f32, M = 128, N = 128.
+// Instruction descriptor: f16 x f16 -> f32 accumulate, M = 128, N = 128,
+// operand majorness per argument (0 = K-major, 1 = MN-major).
 __host__ __device__ constexpr uint32_t umma_idesc_f16(uint32_t a_mn_major, uint32_t b_mn_major) {
   return (1u << 4) | (a_mn_major << 15) | (b_mn_major << 16) | ((uint32_t)(kBN >> 3) << 17) |
          ((uint32_t)(kBM >> 4) << 24);
 }
 
+struct PrefillParams {
+  int batch, hq, hk, group, seq_len, npairs, units;
+  float scale_log2;
+  __half* o;
+  int64_t os[4];
+  int* err;
+};
+
 struct PfBarriers {
-  uint64_t q_full;
+  uint64_t q_full[2], q_empty[2];
   uint64_t k_full[kPfStages], k_empty[kPfStages];
   uint64_t v_full[kPfStages], v_empty[kPfStages];
-  uint64_t s_full[2], p_full[2], o_full[2];
+  uint64_t s_full[2], p_full[2], o_full[2], o_empty[2];
   uint64_t mma_done;
   uint32_t tmem_base;
 };
 
+// One work unit = 256 consecutive query rows (two 128-row tiles) of one head.
+struct PfUnit {
+  int b, h, hk, pair;
+  int n[2];  // KV tiles each Q tile needs (0 = tile beyond seq_len)
+  int nkv;   // KV tiles the unit streams = max(n[0], n[1])
+};
+
+// Units are numbered longest-first (largest pair index first; the heads of one
+// KV group adjacent, so they share K/V in L2). Persistent CTA c of G takes unit
+// k = r*G + (r even ? c : G-1-c) in round r — a snake order that keeps the
+// per-CTA total work within one unit of greedy longest-processing-time.
+__device__ __forceinline__ int pf_unit_index(int round, int cta, int G) {
+  return round * G + ((round & 1) ? (G - 1 - cta) : cta);
+}
+
+__device__ __forceinline__ PfUnit pf_unit(const PrefillParams& p, int k) {
+  PfUnit u;
+  const int per_pair = p.batch * p.hq;
+  u.pair = p.npairs - 1 - k / per_pair;
+  const int rem = k % per_pair;
+  u.b = rem / p.hq;
+  u.h = rem % p.hq;
+  u.hk = u.h / p.group;
+  for (int t = 0; t < 2; ++t) {
+    const int r0 = u.pair * 2 * kBM + t * kBM;
+    u.n[t] = r0 < p.seq_len ? r0 / kBN + 1 : 0;
+  }
+  u.nkv = u.n[1] > 0 ? u.n[1] : u.n[0];
+  return u;
+}
+
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k,
-                       const __grid_constant__ CUtensorMap tm_v,
-                       const __grid_constant__ CUtensorMap tm_o, const PrefillParams p) {
+                       const __grid_constant__ CUtensorMap tm_v, const PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -92,38 +149,26 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   PfBarriers* bars = reinterpret_cast<PfBarriers*>(sV + kPfStages * kTileBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  // Work unit: longest (largest pair index) first; heads of one KV group adjacent.
-  const int per_pair = p.batch * p.hq;
-  const int pair = p.npairs - 1 - (int)(blockIdx.x / per_pair);
-  const int rem = (int)(blockIdx.x % per_pair);
-  const int b = rem / p.hq, h = rem % p.hq;
-  const int hk = h / p.group;
-  int n_tiles[2];
-  bool live[2];
-  for (int t = 0; t < 2; ++t) {
-    const int r0 = pair * 2 * kBM + t * kBM;
-    live[t] = r0 < p.seq_len;
-    n_tiles[t] = live[t] ? r0 / kBN + 1 : 0;
-  }
-  const int nkv = live[1] ? n_tiles[1] : n_tiles[0];
+  const int G = gridDim.x, cta = blockIdx.x;
 
   if (warp == 0) {
     tmem_alloc(&bars->tmem_base, 512);
     tmem_relinquish();
   }
   if (threadIdx.x == 32) {
-    mbar_init(&bars->q_full, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&bars->q_full[t], 1);
+      mbar_init(&bars->q_empty[t], 1);
+      mbar_init(&bars->s_full[t], 1);
+      mbar_init(&bars->p_full[t], 4);
+      mbar_init(&bars->o_full[t], 1);
+      mbar_init(&bars->o_empty[t], 4);
+    }
     for (int s = 0; s < kPfStages; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->k_empty[s], 1);
       mbar_init(&bars->v_full[s], 1);
       mbar_init(&bars->v_empty[s], 1);
-    }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(&bars->s_full[t], 1);
-      mbar_init(&bars->p_full[t], 4);
-      mbar_init(&bars->o_full[t], 1);
     }
     mbar_init(&bars->mma_done, 1);
     fence_barrier_init();
@@ -133,218 +178,283 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
-  if (warp == 8) {
-    // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
+  if (warp >= 8) {
+    // Warpgroup 2 gives registers to the softmax warpgroups, runs the producer
+    // and UMMA roles (lane 0 of warps 8 and 9) and leaves through its own exit:
+    // every .sync.aligned instruction below is reached by whole, converged warps.
+    setmaxnreg_dec<kRegsOther>();
+    if (warp == 8 && lane == 0) {
+      // ---------------------------------------------------------- TMA producer
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_k);
       prefetch_tmap(&tm_v);
-      const int q_bytes = (live[0] ? kTileBytes : 0) + (live[1] ? kTileBytes : 0);
-      mbar_arrive_expect_tx(&bars->q_full, q_bytes);
-      for (int t = 0; t < 2; ++t) {
-        if (!live[t]) continue;
-        const int r0 = pair * 2 * kBM + t * kBM;
-        tma_load_4d(sQ + t * kTileBytes, &tm_q, &bars->q_full, 0, r0, h, b);
-        tma_load_4d(sQ + t * kTileBytes + kHalfBytes, &tm_q, &bars->q_full, 64, r0, h, b);
+      int qc[2] = {0, 0};  // Q loads per tile so far
+      int g = 0;           // K/V tiles streamed so far (all units)
+      bool ok = true;
+      for (int r = 0; ok; ++r) {
+        const int k = pf_unit_index(r, cta, G);
+        if (k >= p.units) break;
+        const PfUnit u = pf_unit(p, k);
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (u.n[t] == 0) continue;
+          if (qc[t] > 0) ok = mbar_wait(&bars->q_empty[t], (qc[t] - 1) & 1, p.err);
+          if (!ok) break;
+          const int r0 = u.pair * 2 * kBM + t * kBM;
+          mbar_arrive_expect_tx(&bars->q_full[t], kTileBytes);
+          tma_load_4d(sQ + t * kTileBytes, &tm_q, &bars->q_full[t], 0, r0, u.h, u.b);
+          tma_load_4d(sQ + t * kTileBytes + kHalfBytes, &tm_q, &bars->q_full[t], 64, r0, u.h, u.b);
+          ++qc[t];
+        }
+        for (int j = 0; ok && j < u.nkv; ++j, ++g) {
+          const int s = g % kPfStages;
+          const uint32_t par = ((g / kPfStages) - 1) & 1;
+          if (g >= kPfStages && !(ok = mbar_wait(&bars->k_empty[s], par, p.err))) break;
+          mbar_arrive_expect_tx(&bars->k_full[s], kTileBytes);
+          tma_load_4d(sK + s * kTileBytes, &tm_k, &bars->k_full[s], 0, j * kBN, u.hk, u.b);
+          tma_load_4d(sK + s * kTileBytes + kHalfBytes, &tm_k, &bars->k_full[s], 64, j * kBN, u.hk, u.b);
+          if (g >= kPfStages && !(ok = mbar_wait(&bars->v_empty[s], par, p.err))) break;
+          mbar_arrive_expect_tx(&bars->v_full[s], kTileBytes);
+          tma_load_4d(sV + s * kTileBytes, &tm_v, &bars->v_full[s], 0, j * kBN, u.hk, u.b);
+          tma_load_4d(sV + s * kTileBytes + kHalfBytes, &tm_v, &bars->v_full[s], 64, j * kBN, u.hk, u.b);
+        }
       }
-      for (int j = 0; j < nkv; ++j) {
-        const int s = j % kPfStages;
-        const uint32_t par = ((j / kPfStages) - 1) & 1;
-        if (j >= kPfStages && !mbar_wait(&bars->k_empty[s], par, p.err)) break;
-        mbar_arrive_expect_tx(&bars->k_full[s], kTileBytes);
-        tma_load_4d(sK + s * kTileBytes, &tm_k, &bars->k_full[s], 0, j * kBN, hk, b);
-        tma_load_4d(sK + s * kTileBytes + kHalfBytes, &tm_k, &bars->k_full[s], 64, j * kBN, hk, b);
-        if (j >= kPfStages && !mbar_wait(&bars->v_empty[s], par, p.err)) break;
-        mbar_arrive_expect_tx(&bars->v_full[s], kTileBytes);
-        tma_load_4d(sV + s * kTileBytes, &tm_v, &bars->v_full[s], 0, j * kBN, hk, b);
-        tma_load_4d(sV + s * kTileBytes + kHalfBytes, &tm_v, &bars->v_full[s], 64, j * kBN, hk, b);
-      }
-    }
-  } else if (warp == 9) {
-    // ------------------------------------------------------------ UMMA issuer
-    if (lane == 0) {
+    } else if (warp == 9 && lane == 0) {
+      // ---------------------------------------------------------- UMMA issuer
       constexpr uint32_t idesc_qk = umma_idesc_f16(0, 0);
       constexpr uint32_t idesc_pv = umma_idesc_f16(0, 1);
       const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-      bool ok = mbar_wait(&bars->q_full, 0, p.err);
-      auto issue_s = [&](int t, int j) {
-        const uint32_t qa = q_addr + t * kTileBytes;
-        const uint32_t ka = k_addr + (j % kPfStages) * kTileBytes;
+      int qc[2] = {0, 0};   // units seen per tile (q_full / o_full / o_empty phases)
+      int sc[2] = {0, 0};   // S tiles issued per tile (s_full / p_full phases)
+      int g = 0;            // K/V tiles consumed so far
+      bool ok = true;
+      // Descriptors are built once per operand; a K step only advances the start
+      // address field (16-byte units, no carry: shared addresses are < 2^18).
+      auto issue_s = [&](int t, int kstage) {
+        const uint64_t da = umma_desc_sw128(q_addr + t * kTileBytes, 16, 1024);
+        const uint64_t db = umma_desc_sw128(k_addr + kstage * kTileBytes, 16, 1024);
 #pragma unroll
-        for (int k = 0; k < kHD / 16; ++k) {
-          const uint32_t off = (k >> 2) * kHalfBytes + (k & 3) * 32;
-          umma_ss(tmem + t * kBN, umma_desc_sw128(qa + off, 16, 1024),
-                  umma_desc_sw128(ka + off, 16, 1024), idesc_qk, k > 0);
+        for (int kk = 0; kk < kHD / 16; ++kk) {
+          const uint32_t off = ((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4;
+          umma_ss(tmem + t * kBN, da + off, db + off, idesc_qk, kk > 0);
         }
         umma_commit(&bars->s_full[t]);
       };
-      auto issue_pv = [&](int t, int j) {
-        const uint32_t va = v_addr + (j % kPfStages) * kTileBytes;
+      auto issue_pv = [&](int t, int vstage, bool first) {
+        const uint64_t db = umma_desc_sw128(v_addr + vstage * kTileBytes, kHalfBytes, 1024);
 #pragma unroll
-        for (int k = 0; k < kBN / 16; ++k) {
-          umma_ts(tmem + 256 + t * kHD, tmem + t * kBN + k * 8,
-                  umma_desc_sw128(va + k * 16 * 128, kHalfBytes, 1024), idesc_pv,
-                  (j > 0 || k > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          umma_ts(tmem + 256 + t * kHD, tmem + t * kBN + kk * 8, db + (uint32_t)(kk * 16 * 128 / 16),
+                  idesc_pv, (!first || kk > 0) ? 1u : 0u);
         }
       };
-      if (ok && nkv > 0) {
-        ok = mbar_wait(&bars->k_full[0], 0, p.err);
-        if (ok) {
-          tc_fence_after();
-          for (int t = 0; t < 2; ++t)
-            if (live[t]) issue_s(t, 0);
-        }
-      }
-      for (int j = 0; ok && j < nkv; ++j) {
-        const bool has_next = j + 1 < nkv;
-        if (has_next) {
-          ok = mbar_wait(&bars->k_full[(j + 1) % kPfStages], ((j + 1) / kPfStages) & 1, p.err);
-          if (!ok) break;
-        }
-        ok = mbar_wait(&bars->v_full[j % kPfStages], (j / kPfStages) & 1, p.err);
-        if (!ok) break;
-        tc_fence_after();
+      for (int r = 0; ok; ++r) {
+        const int k = pf_unit_index(r, cta, G);
+        if (k >= p.units) break;
+        const PfUnit u = pf_unit(p, k);
+        // First K tile of the unit, then S_t(0) for each live tile.
+        ok = mbar_wait(&bars->k_full[g % kPfStages], (g / kPfStages) & 1, p.err);
         for (int t = 0; t < 2 && ok; ++t) {
-          if (!live[t] || j >= n_tiles[t]) continue;
-          ok = mbar_wait(&bars->p_full[t], j & 1, p.err);
+          if (u.n[t] == 0) continue;
+          ok = mbar_wait(&bars->q_full[t], qc[t] & 1, p.err);
           if (!ok) break;
           tc_fence_after();
-          issue_pv(t, j);
-          if (j == n_tiles[t] - 1)
-            umma_commit(&bars->o_full[t]);
-          else
-            issue_s(t, j + 1);
+          issue_s(t, g % kPfStages);
+          ++sc[t];
+          if (u.n[t] == 1) umma_commit(&bars->q_empty[t]);
         }
-        umma_commit(&bars->v_empty[j % kPfStages]);
-        if (has_next) umma_commit(&bars->k_empty[(j + 1) % kPfStages]);
-        // K tile 0 is only released here once tile-0/1 S MMAs of j = 0 finished.
-        if (j == 0) umma_commit(&bars->k_empty[0]);
+        for (int j = 0; ok && j < u.nkv; ++j, ++g) {
+          const bool has_next = j + 1 < u.nkv;
+          if (has_next) {
+            ok = mbar_wait(&bars->k_full[(g + 1) % kPfStages], ((g + 1) / kPfStages) & 1, p.err);
+            if (!ok) break;
+          }
+          ok = mbar_wait(&bars->v_full[g % kPfStages], (g / kPfStages) & 1, p.err);
+          if (!ok) break;
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (j >= u.n[t]) continue;
+            ok = crit_wait(&bars->p_full[t], (sc[t] - 1) & 1, p.err);
+            // PV_t(0) overwrites O_t: the previous unit's epilogue must have read it.
+            if (ok && j == 0 && qc[t] > 0)
+              ok = mbar_wait(&bars->o_empty[t], (qc[t] - 1) & 1, p.err);
+            if (!ok) break;
+            tc_fence_after();
+            issue_pv(t, g % kPfStages, j == 0);
+            if (j == u.n[t] - 1) {
+              umma_commit(&bars->o_full[t]);
+            } else {
+              issue_s(t, (g + 1) % kPfStages);
+              ++sc[t];
+              if (j + 1 == u.n[t] - 1) umma_commit(&bars->q_empty[t]);
+            }
+          }
+          umma_commit(&bars->v_empty[g % kPfStages]);
+          // Free each K stage as soon as the S MMAs reading it complete: K tile g+1
+          // was read by the S(j+1) issued above, the unit's first K tile by S(0).
+          if (j == 0) umma_commit(&bars->k_empty[g % kPfStages]);
+          if (has_next) umma_commit(&bars->k_empty[(g + 1) % kPfStages]);
+        }
+        for (int t = 0; t < 2; ++t)
+          if (u.n[t] > 0) ++qc[t];
       }
       umma_commit(&bars->mma_done);
       mbar_wait(&bars->mma_done, 0, p.err);
     }
-  } else {
-    // ------------------------------------------- softmax + epilogue, warps 0-7
+    __syncwarp();
+    named_bar_arrive(kTeardownBar, kPfThreads);
+    return;
+  }
+
+  // ------------------------------------------- softmax + epilogue, warps 0-7
+  setmaxnreg_inc<kRegsSoftmax>();
+  {
     const int t = warp >> 2;             // Q tile of this warpgroup
     const int quarter = warp & 3;        // TMEM lane quarter
     const int row = quarter * 32 + lane; // row within the tile
-    const int r0 = pair * 2 * kBM + t * kBM;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t tS = tmem + lane_off + t * kBN;
     const uint32_t tO = tmem + lane_off + 256 + t * kHD;
     const float sl2 = p.scale_log2;
-    const int n_my = t ? n_tiles[1] : n_tiles[0];
-    float m = -INFINITY, l = 0.f;
-    bool ok = t ? live[1] : live[0];
-    for (int j = 0; ok && j < n_my; ++j) {
-      ok = mbar_wait(&bars->s_full[t], j & 1, p.err);
+    int sc = 0;  // S tiles consumed (s_full / p_full phases)
+    int uc = 0;  // units finished (o_full / o_empty phases)
+    bool ok = true;
+    for (int r = 0; ok; ++r) {
+      const int k = pf_unit_index(r, cta, G);
+      if (k >= p.units) break;
+      const PfUnit u = pf_unit(p, k);
+      const int n_my = u.n[t];
+      if (n_my == 0) continue;
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; ok && j < n_my; ++j, ++sc) {
+        ok = __all_sync(0xffffffffu, crit_wait(&bars->s_full[t], sc & 1, p.err));
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t sr[kBN];
+        tmem_ld32(tS + 0, sr + 0);
+        tmem_ld32(tS + 32, sr + 32);
+        tmem_ld32(tS + 64, sr + 64);
+        tmem_ld32(tS + 96, sr + 96);
+        tmem_wait_ld();
+        reg_fence<kBN>(sr);
+        if (j == n_my - 1) {
+          // Diagonal tile: key column c (absolute r0 + c) is visible iff c <= row.
+#pragma unroll
+          for (int c = 0; c < kBN; ++c)
+            if (c > row) sr[c] = __float_as_uint(-INFINITY);
+        }
+        // Row max as 8 independent chains of 3-input max (short dependency chains).
+        float mx8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float a = __uint_as_float(sr[i]);
+#pragma unroll
+          for (int kk = 1; kk < 15; kk += 2)
+            a = fmax3f(a, __uint_as_float(sr[i + 8 * kk]), __uint_as_float(sr[i + 8 * (kk + 1)]));
+          mx8[i] = fmaxf(a, __uint_as_float(sr[i + 120]));
+        }
+        const float mx = fmaxf(fmax3f(mx8[0], mx8[1], mx8[2]),
+                               fmax3f(fmax3f(mx8[3], mx8[4], mx8[5]), mx8[6], mx8[7]));
+        const float m_tile = mx * sl2;
+        const float m_new = fmaxf(m, m_tile);
+        // Lazy rescale: only rows whose max grew by more than the threshold move
+        // their reference point (and then O_t and l are rescaled by alpha).
+        bool rescale = false;
+        float alpha = 1.f;
+        if (j == 0) {
+          m = m_new;
+        } else {
+          const bool need = m_new > m + kRescaleThreshold;
+          rescale = __any_sync(0xffffffffu, need);
+          if (need) {
+            alpha = fast_exp2(m - m_new);
+            m = m_new;
+            l *= alpha;
+          }
+        }
+        const float mref = (m == -INFINITY) ? 0.f : m;
+        // p = 2^(s*scale_log2 - m): scaling on packed FFMA2, exp2 on MUFU (and on the
+        // FMA pipe for a share of the columns), row sum in 4 packed FADD2 chains;
+        // P packed in place (entry c/2 written after entries c and c+1 were read).
+        const uint64_t sc2 = f32x2(sl2, sl2), nm2 = f32x2(-mref, -mref);
+        uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+        for (int c = 0; c < kBN; c += 2) {
+          const uint64_t xp =
+              fma_f32x2(f32x2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), sc2, nm2);
+          float p0, p1;
+          if (((c >> 1) & 7) < kEmuPairsPer8) {
+            exp2_poly_x2(xp, p0, p1);
+          } else {
+            float x0, x1;
+            f32x2_split(xp, x0, x1);
+            p0 = fast_exp2(x0);
+            p1 = fast_exp2(x1);
+          }
+          sum2[(c >> 1) & 3] = add_f32x2(sum2[(c >> 1) & 3], f32x2(p0, p1));
+          sr[c >> 1] = pack_half2(p0, p1);
+        }
+        {
+          const uint64_t s01 =
+              add_f32x2(add_f32x2(sum2[0], sum2[1]), add_f32x2(sum2[2], sum2[3]));
+          float lo, hi;
+          f32x2_split(s01, lo, hi);
+          l += lo + hi;
+        }
+        tmem_st32(tS + 0, sr);
+        tmem_st32(tS + 32, sr + 32);
+        if (rescale) {
+          // PV_t(j-1) is complete: s_full for step j was committed after it.
+#pragma unroll
+          for (int cc = 0; cc < kHD; cc += 32) {
+            uint32_t ov[32];
+            tmem_ld32(tO + cc, ov);
+            tmem_wait_ld();
+            reg_fence<32>(ov);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+            tmem_st32(tO + cc, ov);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_full[t]);
+      }
+      // ----------------------------------------------------------- epilogue
+      // O_t -> registers (then O_t is released for the next unit's first PV),
+      // normalise, and store fp16 rows straight to global memory.
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_full[t], uc & 1, p.err));
       if (!ok) break;
       tc_fence_after();
-      uint32_t sr[kBN];
-      tmem_ld32(tS + 0, sr + 0);
-      tmem_ld32(tS + 32, sr + 32);
-      tmem_ld32(tS + 64, sr + 64);
-      tmem_ld32(tS + 96, sr + 96);
+      uint32_t ov[kHD];
+      tmem_ld32(tO + 0, ov + 0);
+      tmem_ld32(tO + 32, ov + 32);
+      tmem_ld32(tO + 64, ov + 64);
+      tmem_ld32(tO + 96, ov + 96);
       tmem_wait_ld();
-      reg_fence<kBN>(sr);
-      if (j == n_my - 1) {
-        // Diagonal tile: key column c (absolute r0 + c) is visible iff c <= row.
-#pragma unroll
-        for (int c = 0; c < kBN; ++c)
-          if (c > row) sr[c] = __float_as_uint(-INFINITY);
-      }
-      float mx = __uint_as_float(sr[0]);
-#pragma unroll
-      for (int c = 1; c < kBN; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
-      const float m_tile = mx * sl2;
-      const float m_new = fmaxf(m, m_tile);
-      // Lazy rescale: only rows whose max grew by more than the threshold move
-      // their reference point (and then O_t and l are rescaled by alpha).
-      bool rescale = false;
-      float alpha = 1.f;
-      if (j == 0) {
-        m = m_new;
-      } else {
-        const bool need = m_new > m + kRescaleThreshold;
-        rescale = __any_sync(0xffffffffu, need);
-        if (need) {
-          alpha = fast_exp2(m - m_new);
-          m = m_new;
-          l *= alpha;
-        }
-      }
-      const float mref = (m == -INFINITY) ? 0.f : m;
-      float rs = 0.f;
-      // P packed in place: entry c/2 is written after entries c and c+1 were read.
-#pragma unroll
-      for (int c = 0; c < kBN; c += 2) {
-        const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c]), sl2, -mref));
-        const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c + 1]), sl2, -mref));
-        rs += p0 + p1;
-        sr[c >> 1] = pack_half2(p0, p1);
-      }
-      l += rs;
-      tmem_st32(tS + 0, sr);
-      tmem_st32(tS + 32, sr + 32);
-      if (rescale) {
-        // PV_t(j-1) is complete: s_full for step j was committed after it.
-#pragma unroll
-        for (int cc = 0; cc < kHD; cc += 32) {
-          uint32_t ov[32];
-          tmem_ld32(tO + cc, ov);
-          tmem_wait_ld();
-          reg_fence<32>(ov);
-#pragma unroll
-          for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-          tmem_st32(tO + cc, ov);
-        }
-      }
-      tmem_wait_st();
+      reg_fence<kHD>(ov);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full[t]);
-    }
-    // ------------------------------------------------------------- epilogue
-    if (ok) ok = mbar_wait(&bars->o_full[t], 0, p.err);
-    if (ok) {
-      tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      uint8_t* so = sQ + t * kTileBytes;  // Q tile is dead once O is complete
+      if (lane == 0) mbar_arrive(&bars->o_empty[t]);
+      ++uc;
+      const int grow = u.pair * 2 * kBM + t * kBM + row;
+      if (grow < p.seq_len) {
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        __half* orow = p.o + u.b * p.os[0] + u.h * p.os[1] + (int64_t)grow * p.os[2];
 #pragma unroll
-      for (int cc = 0; cc < kHD; cc += 32) {
-        uint32_t ov[32];
-        tmem_ld32(tO + cc, ov);
-        tmem_wait_ld();
-        reg_fence<32>(ov);
-        uint32_t hv[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e)
-          hv[e] = pack_half2(__uint_as_float(ov[2 * e]) * inv, __uint_as_float(ov[2 * e + 1]) * inv);
-        const int half = cc >> 6;
-        const uint32_t base = smem_u32(so + half * kHalfBytes) + row * 128;
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const int chunk = ((cc & 63) >> 3) + q4;
-          const uint32_t addr = base + ((chunk ^ (row & 7)) << 4);
-          asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr),
-                       "r"(hv[4 * q4]), "r"(hv[4 * q4 + 1]), "r"(hv[4 * q4 + 2]),
-                       "r"(hv[4 * q4 + 3])
-                       : "memory");
+        for (int c8 = 0; c8 < kHD; c8 += 8) {
+          uint4 pk;
+          pk.x = pack_half2(__uint_as_float(ov[c8 + 0]) * inv, __uint_as_float(ov[c8 + 1]) * inv);
+          pk.y = pack_half2(__uint_as_float(ov[c8 + 2]) * inv, __uint_as_float(ov[c8 + 3]) * inv);
+          pk.z = pack_half2(__uint_as_float(ov[c8 + 4]) * inv, __uint_as_float(ov[c8 + 5]) * inv);
+          pk.w = pack_half2(__uint_as_float(ov[c8 + 6]) * inv, __uint_as_float(ov[c8 + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + c8) = pk;
         }
-      }
-      fence_proxy_async_smem();
-      named_bar_sync(1 + t, 128);
-      if (quarter == 0 && lane == 0) {
-        tma_store_4d(&tm_o, so, 0, r0, h, b);
-        tma_store_4d(&tm_o, so + kHalfBytes, 64, r0, h, b);
-        tma_store_commit();
-        tma_store_wait_all();
       }
     }
   }
 
   tc_fence_before();
-  __syncthreads();
+  named_bar_sync(kTeardownBar, kPfThreads);
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -390,15 +500,18 @@ extern "C" int fi_prefill_fwd(const void* q, const void* k, const void* v, void*
     return fail(FI_ERR_INVALID_ARG, "fi_prefill_fwd: null pointer argument");
   if (seq_len > (1 << 30) || batch > 65535 || num_q_heads > 65535)
     return fail(FI_ERR_UNSUPPORTED, "fi_prefill_fwd: sizes too large");
-  CUtensorMap tq, tk, tv, to;
+  CUtensorMap tq, tk, tv;
   int r = make_bhsd_map(&tq, q, batch, num_q_heads, seq_len, q_strides, "fi_prefill_fwd q");
   if (r != FI_OK) return r;
   r = make_bhsd_map(&tk, k, batch, num_kv_heads, seq_len, k_strides, "fi_prefill_fwd k");
   if (r != FI_OK) return r;
   r = make_bhsd_map(&tv, v, batch, num_kv_heads, seq_len, v_strides, "fi_prefill_fwd v");
   if (r != FI_OK) return r;
-  r = make_bhsd_map(&to, o, batch, num_q_heads, seq_len, o_strides, "fi_prefill_fwd o");
-  if (r != FI_OK) return r;
+  if (o_strides[3] != 1 || (reinterpret_cast<uintptr_t>(o) & 15) != 0 || o_strides[0] % 8 != 0 ||
+      o_strides[1] % 8 != 0 || o_strides[2] % 8 != 0)
+    return fail(FI_ERR_ALIGNMENT,
+                "fi_prefill_fwd o: needs a 16-byte aligned base, unit innermost stride and "
+                "other strides multiple of 8");
 
   PrefillParams p;
   p.batch = (int)batch;
@@ -409,8 +522,12 @@ extern "C" int fi_prefill_fwd(const void* q, const void* k, const void* v, void*
   p.npairs = (int)((seq_len + 2 * kBM - 1) / (2 * kBM));
   p.scale_log2 = (float)((double)sm_scale * 1.4426950408889634);
   p.err = error_flag;
+  p.o = static_cast<__half*>(o);
+  for (int i = 0; i < 4; ++i) p.os[i] = o_strides[i];
   const int64_t units = (int64_t)p.npairs * batch * num_q_heads;
-  if (units > 0x7fffffff) return fail(FI_ERR_UNSUPPORTED, "fi_prefill_fwd: grid too large");
+  if (units > 0x7fffffff) return fail(FI_ERR_UNSUPPORTED, "fi_prefill_fwd: too many work units");
+  p.units = (int)units;
+  const int grid = (int)(units < sm_count() ? units : sm_count());
 
   static bool attr_done[64] = {false};
   int dev = 0;
@@ -421,8 +538,8 @@ extern "C" int fi_prefill_fwd(const void* q, const void* k, const void* v, void*
     if (e != cudaSuccess) return cuda_fail(e, "fi_prefill_fwd: cudaFuncSetAttribute");
     attr_done[dev] = true;
   }
-  prefill_fwd_kernel<<<(unsigned)units, kPfThreads, kPfSmemBytes, static_cast<cudaStream_t>(stream)>>>(
-      tq, tk, tv, to, p);
+  prefill_fwd_kernel<<<(unsigned)grid, kPfThreads, kPfSmemBytes,
+                       static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "fi_prefill_fwd: launch");
   return FI_OK;
