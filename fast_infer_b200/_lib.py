@@ -48,6 +48,9 @@ SIGNATURES = {
     "fi_paged_decode": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                                        _i64, _i64, _i64, _i64, _i64, _i64p, _i64p, _i64p,
                                        _i64p, _i64p, _f32, _i64, _vp, _sz, _vp, _vp]),
+    "fi_paged_decode_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
+                                               _i64, _i64, _i64, _i64, _i64, _i64, _i64p, _i64p,
+                                               _i64p, _i64p, _i64p, _f32, _i64, _vp, _vp]),
     "fi_kv_write": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64,
                                    _i64, _i64, _i64, _i64, _i64p, _i64p, _i64p, _i64p, _i64p,
                                    _vp, _vp]),

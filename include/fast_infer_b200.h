@@ -109,6 +109,33 @@ int fi_paged_decode(const void* q, const void* k_cache, const void* v_cache, voi
                     int32_t* error_flag, void* stream);
 
 /*
+ * Paged decode that allocates nothing: identical arguments and results to
+ * fi_paged_decode minus the workspace, whose split-KV scratch comes from a
+ * file-scope static device array of FI_NOALLOC_SCRATCH_BYTES instead.
+ *
+ * No counterpart in the reference. For callers that cannot allocate device memory
+ * themselves: a C/C++ host linking only this library (no caching allocator, and
+ * cudaMalloc would synchronise the device on the decode path) or a runtime that
+ * forbids allocation after start-up to keep its footprint fixed.
+ *
+ * Sizes needing more scratch than FI_NOALLOC_SCRATCH_BYTES return FI_ERR_WORKSPACE.
+ * Every GPU that loads the library holds the array until exit; all calls on a
+ * device share it, so calls that overlap on the GPU race (order them on one
+ * stream). The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress); make it before any stream capture.
+ */
+#define FI_NOALLOC_SCRATCH_BYTES (16 * 1024 * 1024)
+int fi_paged_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, void* o,
+                            const int32_t* block_table, const int32_t* context_lens,
+                            int64_t num_tokens, int64_t max_context_len, int64_t batch,
+                            int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
+                            int64_t num_blocks, int64_t block_size, int64_t max_blocks_per_seq,
+                            const int64_t* q_strides, const int64_t* kc_strides,
+                            const int64_t* vc_strides, const int64_t* o_strides,
+                            const int64_t* bt_strides, float sm_scale, int64_t pages_per_split,
+                            int32_t* error_flag, void* stream);
+
+/*
  * KV-cache slot write: copy new tokens' K and V rows into their pages.
  *
  * Replaces: the slot writes of model.py:162-183 (`_store_kv_prefill`), model.py:185-201
