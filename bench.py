@@ -270,7 +270,6 @@ def run_ours(args):
     d2h = ho.numel() * 2
 
     # ---- prefill, config 2 (B4 x S2048, 24/8, seed 1); 4 rotating input sets > L2
-    from fast_infer_b200.kernels.attention import flash_attention
     sets = prefill_inputs(torch, dev, 4)
     pf_steps = max(args.steps // 4, 10)
     lib = _lib.load()
@@ -284,6 +283,8 @@ def run_ours(args):
     wl3 = DecodeWorkload(torch, dev, C3_SEQS, C3_LO, C3_HI, C3_SEED + rank, 8)
     ms3 = timed(torch, lambda i: wl3.attend(i % 8), args.steps, args.warmup, dist) / args.steps
     c3_gbs = wl3.bytes / (ms3 * 1e-3) / 1e9
+
+    stack = run_stack(torch, dev, rank, world, dist) if not args.no_stack else None
 
     launches_per_step = 2 + (1 if _needs_combine(wl) else 0)
     result = {
@@ -328,6 +329,7 @@ def run_ours(args):
             "ms": round(ms3, 4), "gbs": round(c3_gbs, 1),
             "frac": round(c3_gbs / hbm_peak, 4),
         },
+        "stack": stack,
         "e2e": {
             "value": round(total_bytes / (e2e_step_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
             "ms_per_step": round(e2e_step_ms, 5),
@@ -378,7 +380,9 @@ def run_only(args):
     lib = load()
     peaks, peak_kind = load_peaks()
     out = {"only": args.only, "steps": args.steps, "warmup": args.warmup}
-    if args.only == "prefill":
+    if args.only == "stack":
+        out.update(run_stack(torch, dev, 0, 1, None))
+    elif args.only == "prefill":
         sets = prefill_inputs(torch, dev, 4)
         ms = timed(torch, lambda i: prefill_call(torch, lib, sets[i % 4]), args.steps,
                    args.warmup) / args.steps
@@ -395,6 +399,71 @@ def run_only(args):
         out.update(ms=round(ms, 4), gbs=round(gbs, 1), bytes=wl.bytes,
                    frac=round(gbs / float(peaks["hbm_gbs"]), 4))
     print(json.dumps(out))
+
+
+STACK_LAYERS, STACK_BATCH, STACK_PROMPT, STACK_STEPS = 28, 16, 1024, 256
+
+
+def run_stack(torch, dev, rank, world, dist, warmup=1):
+    """Config 4: 28-layer attention stack (hidden 3072, 24/8 heads, RoPE 5e5, random
+    N(0,0.02) fp16 weights), batch 16, prefill 1024 tokens then 256 decode steps,
+    KV heads sharded over the ranks (all-gather of head outputs before the
+    replicated O projection). Returns prefill / decode tokens/s of the whole job."""
+    from fast_infer_b200.stack import AttentionStack
+    st = AttentionStack(num_layers=STACK_LAYERS, batch=STACK_BATCH,
+                        max_seq_len=STACK_PROMPT + STACK_STEPS, rank=rank, world=world,
+                        device=dev, seed=4)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    prompt = (torch.randn(STACK_BATCH, STACK_PROMPT, 3072, device=dev, generator=g) * 0.5).half()
+    use_graph = True
+    for _ in range(warmup):
+        try:
+            st.generate(prompt[:, :256], 4, use_graph=use_graph)
+        except RuntimeError:
+            st.release_graph()
+            use_graph = False  # capture not possible here: time the same launches eagerly
+            st.generate(prompt[:, :256], 4, use_graph=False)
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_ms(ms):
+        if dist is None:
+            return ms
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    sync_all()
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    e[0].record()
+    h = st.prefill(prompt)[:, -1:]
+    e[1].record()
+    st.begin_decode(h)
+    for _ in range(STACK_STEPS):
+        h = st.decode_step(use_graph=use_graph)
+    e[2].record()
+    torch.cuda.synchronize()
+    pf_ms, dec_ms = max_ms(e[0].elapsed_time(e[1])), max_ms(e[1].elapsed_time(e[2]))
+    finite = bool(torch.isfinite(h).all().item())
+    st.release_graph()
+    sync_all()
+    return {
+        "workload": "config 4: 28-layer attention stack (Llama-3.2-3B attention shapes, random "
+                    "weights), B16, prefill 1024 then 256 decode steps, KV heads sharded over "
+                    f"{world} GPU(s), NCCL all-gather of head outputs per layer",
+        "scaling": "strong",
+        "prefill_ms": round(pf_ms, 3),
+        "prefill_tokens_per_s": round(STACK_BATCH * STACK_PROMPT / (pf_ms * 1e-3), 1),
+        "decode_ms_per_step": round(dec_ms / STACK_STEPS, 4),
+        "decode_tokens_per_s": round(STACK_BATCH * STACK_STEPS / (dec_ms * 1e-3), 1),
+        "cuda_graph": use_graph,
+        "finite": finite,
+    }
 
 
 def _needs_combine(wl):
@@ -489,7 +558,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["decode", "decode_c3", "prefill"], default=None,
+    ap.add_argument("--no-stack", action="store_true", help="skip the config-4 stack section")
+    ap.add_argument("--only", choices=["decode", "decode_c3", "prefill", "stack"], default=None,
                     help="time one kernel family alone (profiling runs); prints one JSON line")
     ap.add_argument("--layers", type=int, default=DECODE_LAYERS,
                     help="resident KV-cache layers of the decode workload")

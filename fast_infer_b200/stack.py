@@ -1,0 +1,255 @@
+"""Multi-layer attention stack on the B200 path (the config-4 harness).
+
+A Llama-3.2-3B-shaped stack of attention blocks — per layer
+RMSNorm -> QKV projection -> RoPE -> causal attention -> O projection -> residual —
+run the way the reference model runs them (model.py:77-135): prefill of a whole
+prompt through ``flash_attention`` plus the KV slot write, then one token per step
+through the slot write plus ``paged_attention`` over the paged cache. The MLP half
+of each decoder layer is not part of this harness (it is not on the attention path).
+
+Sharding by KV head (``fast_infer_b200.shard``): rank r of N holds the QKV weight
+columns of its KV heads and their query heads, and a KV cache with Hkv/N heads;
+attention needs no exchange; the per-rank attention outputs [tokens, Hq/N * D] are
+all-gathered (NCCL) into [tokens, Hq * D] before the O projection, which every rank
+applies in full (replicated), so every rank carries the whole hidden state.
+
+Decode is autoregressive in hidden space: the stack's output for token t is the
+input of token t+1 (there is no embedding or sampler in an attention-only stack).
+Weights are random N(0, 0.02) fp16 drawn on the device from a fixed seed, identical
+on every rank (same GPU model), then sliced to the rank's heads.
+
+The projections, RMSNorm and RoPE use PyTorch (cuBLAS GEMMs); they are outside
+the path this library implements. RMSNorm follows reference
+kernels/rms_norm.py:8-43 (fp32 math, fp16 out); RoPE follows kernels/rope.py:9-44
+(rotate-half form, tables for max_seq_len positions).
+"""
+
+from __future__ import annotations
+
+from typing import Callable, Optional
+
+import torch
+
+from fast_infer_b200._runtime import device_checks
+from fast_infer_b200.kernels.attention import flash_attention, paged_attention
+from fast_infer_b200.kv_cache import KVCache, store_kv_decode, store_kv_prefill
+from fast_infer_b200.shard import HeadShard, gather_heads, head_shard
+
+
+def precompute_freqs(head_dim: int, max_seq_len: int, theta: float, device) -> tuple:
+    """cos/sin tables [max_seq_len, head_dim] (reference kernels/rope.py:9-16)."""
+    freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2, device=device).float() / head_dim))
+    pos = torch.arange(max_seq_len, device=device).float()
+    ang = torch.outer(pos, freq)
+    ang = torch.cat([ang, ang], dim=-1)
+    return ang.cos(), ang.sin()
+
+
+def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """x * cos + rotate_half(x) * sin for x [B, S, H, D], cos/sin [S, D] fp16
+    (reference kernels/rope.py:19-44)."""
+    d = x.shape[-1]
+    rot = torch.cat([-x[..., d // 2:], x[..., : d // 2]], dim=-1)
+    return x * cos.unsqueeze(1) + rot * sin.unsqueeze(1)
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """x * rsqrt(mean(x^2) + eps) * w in fp32, fp16 out (reference kernels/rms_norm.py)."""
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(x.dtype)
+
+
+class AttentionStack:
+    """``num_layers`` attention blocks of the config-4 shape, sharded by KV head."""
+
+    def __init__(self, num_layers: int = 28, hidden: int = 3072, num_q_heads: int = 24,
+                 num_kv_heads: int = 8, head_dim: int = 128, rope_theta: float = 500000.0,
+                 rms_eps: float = 1e-5, batch: int = 16, max_seq_len: int = 1280,
+                 rank: int = 0, world: int = 1, device=None, seed: int = 0,
+                 gather: Optional[Callable[[torch.Tensor], torch.Tensor]] = None):
+        self.device = torch.device(device or "cuda")
+        self.L, self.hidden, self.D = num_layers, hidden, head_dim
+        self.hq, self.hkv = num_q_heads, num_kv_heads
+        self.eps = rms_eps
+        self.batch = batch
+        self.shard: HeadShard = head_shard(rank, world, num_q_heads, num_kv_heads)
+        self.world = world
+        self.gather = gather if gather is not None else gather_heads
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed)
+        dev = self.device
+        sh = self.shard
+        self.layers = []
+        for _ in range(num_layers):
+            # full weights drawn identically on every rank, then sliced to the shard
+            wq = torch.randn(hidden, num_q_heads * head_dim, generator=g, device=dev) * 0.02
+            wk = torch.randn(hidden, num_kv_heads * head_dim, generator=g, device=dev) * 0.02
+            wv = torch.randn(hidden, num_kv_heads * head_dim, generator=g, device=dev) * 0.02
+            wo = torch.randn(num_q_heads * head_dim, hidden, generator=g, device=dev) * 0.02
+            norm = 1.0 + 0.1 * torch.randn(hidden, generator=g, device=dev)
+            q_cols = slice(sh.q_start * head_dim, sh.q_end * head_dim)
+            kv_cols = slice(sh.kv_start * head_dim, sh.kv_end * head_dim)
+            wqkv = torch.cat([wq[:, q_cols], wk[:, kv_cols], wv[:, kv_cols]], dim=1)
+            self.layers.append(dict(norm=norm.half(), wqkv=wqkv.half().contiguous(),
+                                    wo=wo.half().contiguous()))
+        self.cos, self.sin = precompute_freqs(head_dim, max_seq_len, rope_theta, self.device)
+        pages_per_seq = (max_seq_len + 63) // 64
+        self.cache = KVCache(num_layers, sh.num_kv_heads, head_dim, max_seq_len, 64, self.device,
+                             num_blocks=batch * pages_per_seq)
+        self.cache._grow_batch(batch)
+        self.token_count = 0
+
+    def reset(self):
+        self.cache.reset()
+        self.cache._grow_batch(self.batch)
+        self.token_count = 0
+
+    def _gather(self, o: torch.Tensor) -> torch.Tensor:
+        return o if self.world == 1 else self.gather(o)
+
+    # ------------------------------------------------------------------ prefill
+    def _layer_qkv(self, w, h, cos, sin):
+        B, S, _ = h.shape
+        D, nq, nkv = self.D, self.shard.num_q_heads, self.shard.num_kv_heads
+        x = rms_norm(h, w["norm"], self.eps)
+        q, k, v = (x @ w["wqkv"]).split([nq * D, nkv * D, nkv * D], dim=-1)
+        q = apply_rope(q.view(B, S, nq, D), cos, sin)
+        k = apply_rope(k.view(B, S, nkv, D), cos, sin)
+        return q, k, v.view(B, S, nkv, D)
+
+    def prefill(self, h: torch.Tensor) -> torch.Tensor:
+        """Prompt pass (reference model.py:67-69, 108-117): h [B, S, hidden] fp16."""
+        B, S, _ = h.shape
+        self.reset()
+        pos = torch.arange(S, device=self.device)
+        cos, sin = self.cos[pos].half(), self.sin[pos].half()
+        nq = self.shard.num_q_heads
+        for li, w in enumerate(self.layers):
+            q, k, v = self._layer_qkv(w, h, cos, sin)
+            o = flash_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2))
+            store_kv_prefill(self.cache, li, k, v)
+            o = self._gather(o.transpose(1, 2).reshape(B, S, nq * self.D))
+            h = h + o @ w["wo"]
+        self.token_count = S
+        return h
+
+    # ------------------------------------------------------------------- decode
+    def _decode_state(self):
+        """Device-resident step state, so one decode step is a fixed sequence of
+        launches (CUDA-graph capturable): position of the new token, per-sequence
+        context lengths (including it) and write positions."""
+        if getattr(self, "_dev_pos", None) is None:
+            B = self.batch
+            self._dev_pos = torch.zeros(1, dtype=torch.int64, device=self.device)
+            self._dev_ctx = torch.zeros(B, dtype=torch.int32, device=self.device)
+            self._dev_start = torch.zeros(B, dtype=torch.int32, device=self.device)
+            span = self.cache.max_blocks_per_seq * 64
+            from fast_infer_b200.kernels.attention import paged_attention_workspace_bytes
+            need = paged_attention_workspace_bytes(B, self.shard.num_q_heads,
+                                                   self.shard.num_kv_heads, span)
+            self._ws = torch.empty(max(need, 1), dtype=torch.uint8, device=self.device)
+            self._h_in = torch.zeros(B, 1, self.hidden, dtype=torch.float16, device=self.device)
+            self._graph = None
+
+    def _decode_body(self):
+        """One decode token through every layer, reading positions from device
+        memory (reference model.py:70-72, 118-131); advances them at the end."""
+        B = self.batch
+        pos = self._dev_pos
+        cos, sin = self.cos.index_select(0, pos).half(), self.sin.index_select(0, pos).half()
+        nq, D = self.shard.num_q_heads, self.D
+        span = self.cache.max_blocks_per_seq * 64
+        h = self._h_in
+        for li, w in enumerate(self.layers):
+            q, k, v = self._layer_qkv(w, h, cos, sin)
+            self.cache.write_tokens(li, k, v, self._dev_start)
+            o = paged_attention(q[:, 0], self.cache.k[li], self.cache.v[li],
+                                self.cache.block_table, 64, 0, context_lens=self._dev_ctx,
+                                max_context_len=span, workspace=self._ws)
+            o = self._gather(o.reshape(B, 1, nq * D))
+            h = h + o @ w["wo"]
+        self._dev_pos.add_(1)
+        self._dev_ctx.add_(1)
+        self._dev_start.add_(1)
+        self._h_in.copy_(h)
+        return h
+
+    def _host_step(self):
+        """Host bookkeeping before a decode step: allocate a page for every sequence
+        when the new token starts one (reference model.py:193-198)."""
+        pos = self.token_count
+        if pos >= self.cache.max_blocks_per_seq * 64:
+            raise RuntimeError("sequence longer than the stack's max_seq_len")
+        if pos % 64 == 0 or self.cache._dirty:
+            for b in range(self.batch):
+                self.cache._ensure_blocks(b, pos // 64 + 1)
+            self.cache.sync_block_table()
+        self.cache.num_tokens += 1
+        self.token_count += 1
+
+    def begin_decode(self, h_last: torch.Tensor):
+        """Set the decode state after ``prefill``: h_last [B, 1, hidden] is the first
+        decode input; positions continue from the prompt length."""
+        self._decode_state()
+        self._dev_pos.fill_(self.token_count)
+        self._dev_ctx.fill_(self.token_count + 1)
+        self._dev_start.fill_(self.token_count)
+        self._h_in.copy_(h_last)
+
+    def decode_step(self, use_graph: bool = True) -> torch.Tensor:
+        """One decode token for the whole batch; returns the stack output
+        [B, 1, hidden] (a buffer that the next step overwrites)."""
+        self._host_step()
+        if not use_graph:
+            return self._decode_body().clone()
+        if self._graph is None:
+            self._capture()  # captures the step and runs it once
+        else:
+            self._graph.replay()
+        return self._h_out
+
+    def _capture(self):
+        # Save the state, run the body once eagerly (first-call set-up of every
+        # kernel), restore the state, then capture one step.
+        saved = [t.clone() for t in (self._dev_pos, self._dev_ctx, self._dev_start, self._h_in)]
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self._decode_body()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        for t, v in zip((self._dev_pos, self._dev_ctx, self._dev_start, self._h_in), saved):
+            t.copy_(v)
+        g = torch.cuda.CUDAGraph()
+        # reading the device error word synchronises, which a capture forbids
+        with device_checks(False), torch.cuda.graph(g):
+            self._h_out = self._decode_body()
+        self._graph = g
+        # the capture recorded but did not run the step: run it now
+        self._graph.replay()
+
+    def release_graph(self):
+        """Drop the captured decode graph (call before destroying a process group
+        whose collectives it holds)."""
+        self._graph = None
+
+    def forward(self, h: torch.Tensor) -> torch.Tensor:
+        """Reference-style entry (model.py:50-160): S > 1 or the first call = prefill,
+        otherwise one decode token (eager). h: [B, S, hidden] fp16."""
+        if h.shape[1] > 1 or self.token_count == 0:
+            return self.prefill(h)
+        if getattr(self, "_dev_pos", None) is None or self._graph is None:
+            self.begin_decode(h)
+        else:
+            self._h_in.copy_(h)
+        return self.decode_step(use_graph=False)
+
+    def generate(self, prompt_hidden: torch.Tensor, steps: int,
+                 use_graph: bool = True) -> torch.Tensor:
+        """Prefill the prompt, then ``steps`` decode steps each fed with the previous
+        step's output; returns the decode outputs [B, steps, hidden]."""
+        h = self.prefill(prompt_hidden)[:, -1:]
+        self.begin_decode(h)
+        outs = []
+        for _ in range(steps):
+            outs.append(self.decode_step(use_graph=use_graph).clone())
+        return torch.cat(outs, dim=1) if outs else h[:, :0]

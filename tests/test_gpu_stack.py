@@ -1,0 +1,115 @@
+"""The config-4 harness (fast_infer_b200.stack): a multi-layer attention stack on the
+B200 path, checked against the same stack with an fp32 PyTorch attention in place
+of the kernels, and KV-head sharding emulated with two shards on one GPU."""
+
+import threading
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _fp32_attention_stack(stack, prompt, steps):
+    """Same weights and torch ops as AttentionStack, attention = dense fp32 softmax
+    over every cached token (K/V kept as the fp16 values the stack stores)."""
+    from fast_infer_b200.stack import apply_rope, rms_norm
+    B, S, H = prompt.shape
+    D, hq, hkv = stack.D, stack.shard.num_q_heads, stack.shard.num_kv_heads
+    G = hq // hkv
+    ks = [None] * stack.L
+    vs = [None] * stack.L
+
+    def run(h, pos0):
+        n = h.shape[1]
+        pos = torch.arange(pos0, pos0 + n, device=h.device)
+        cos, sin = stack.cos[pos].half(), stack.sin[pos].half()
+        for li, w in enumerate(stack.layers):
+            x = rms_norm(h, w["norm"], stack.eps)
+            q, k, v = (x @ w["wqkv"]).split([hq * D, hkv * D, hkv * D], dim=-1)
+            q = apply_rope(q.view(B, n, hq, D), cos, sin)
+            k = apply_rope(k.view(B, n, hkv, D), cos, sin)
+            v = v.view(B, n, hkv, D)
+            ks[li] = k if ks[li] is None else torch.cat([ks[li], k], 1)
+            vs[li] = v if vs[li] is None else torch.cat([vs[li], v], 1)
+            kk = ks[li].float().repeat_interleave(G, dim=2).transpose(1, 2)
+            vv = vs[li].float().repeat_interleave(G, dim=2).transpose(1, 2)
+            s = (q.float().transpose(1, 2) @ kk.transpose(-1, -2)) * D ** -0.5
+            tot = kk.shape[2]
+            qpos = torch.arange(tot - n, tot, device=h.device)[:, None]
+            s = s.masked_fill(torch.arange(tot, device=h.device)[None, :] > qpos, float("-inf"))
+            o = (torch.softmax(s, -1) @ vv).transpose(1, 2).reshape(B, n, hq * D).half()
+            h = h + o @ w["wo"]
+        return h
+
+    h = run(prompt, 0)[:, -1:]
+    outs = []
+    for t in range(steps):
+        h = run(h, S + t)
+        outs.append(h)
+    return torch.cat(outs, 1)
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm()).item()
+
+
+def test_stack_matches_fp32_attention(cuda_device, device_checks):
+    from fast_infer_b200.stack import AttentionStack
+    torch.manual_seed(0)
+    stack = AttentionStack(num_layers=2, batch=2, max_seq_len=256, device=cuda_device, seed=1)
+    prompt = (torch.randn(2, 70, 3072, device=cuda_device) * 0.5).half()
+    out = stack.generate(prompt, steps=6, use_graph=False)
+    ref = _fp32_attention_stack(stack, prompt, 6)
+    assert out.shape == (2, 6, 3072) and torch.isfinite(out).all()
+    assert _rel(out, ref) < 2e-3
+    # the CUDA-graph decode replays the same launches (cuBLAS may pick other GEMM
+    # algorithms under capture, so compare within tolerance)
+    out_g = stack.generate(prompt, steps=6, use_graph=True)
+    assert _rel(out_g, ref) < 2e-3, _rel(out_g, ref)
+    assert _rel(out_g, out) < 1e-3, _rel(out_g, out)
+    # crossing a page boundary in decode (70 + 6 tokens < 128 -> run longer)
+    out2 = stack.generate(prompt[:, :60], steps=10, use_graph=True)
+    ref2 = _fp32_attention_stack(stack, prompt[:, :60], 10)
+    assert _rel(out2, ref2) < 2e-3
+
+
+def test_kv_head_sharding_matches_unsharded(cuda_device):
+    """Two KV-head shards on one GPU exchange outputs through an in-process
+    all-gather; their result equals the unsharded stack's."""
+    from fast_infer_b200.stack import AttentionStack
+    torch.manual_seed(0)
+    prompt = (torch.randn(2, 65, 3072, device=cuda_device) * 0.5).half()
+    full = AttentionStack(num_layers=2, batch=2, max_seq_len=256, device=cuda_device, seed=3)
+    ref = full.generate(prompt, steps=4, use_graph=False)
+
+    slots = [None, None]
+    bar = threading.Barrier(2)
+
+    def make_gather(rank):
+        def gather(o):
+            slots[rank] = o.contiguous()
+            torch.cuda.synchronize()
+            bar.wait(timeout=60)
+            out = torch.cat([slots[0], slots[1]], dim=-1)
+            bar.wait(timeout=60)
+            return out
+        return gather
+
+    shards = [AttentionStack(num_layers=2, batch=2, max_seq_len=256, device=cuda_device, seed=3,
+                             rank=r, world=2, gather=make_gather(r)) for r in range(2)]
+    results = [None, None]
+
+    def run(r):
+        torch.cuda.set_device(cuda_device)
+        results[r] = shards[r].generate(prompt, steps=4, use_graph=False)
+        torch.cuda.synchronize()
+
+    th = [threading.Thread(target=run, args=(r,)) for r in range(2)]
+    for x in th:
+        x.start()
+    for x in th:
+        x.join(timeout=120)
+    assert results[0] is not None and results[1] is not None
+    assert torch.equal(results[0], results[1])
+    assert _rel(results[0], ref) < 2e-3
