@@ -51,6 +51,9 @@ SIGNATURES = {
     "fi_paged_decode_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
                                                _i64, _i64, _i64, _i64, _i64, _i64, _i64p, _i64p,
                                                _i64p, _i64p, _i64p, _f32, _i64, _vp, _vp]),
+    "fi_rope_kv_write": (ctypes.c_int, [_vp, _i64, _i64, _i64, _i64, _i64, _i64p, _vp, _vp, _i64,
+                                        _i64, _vp, _i64, _vp, _i64p, _vp, _i64p, _vp, _vp, _vp,
+                                        _i64, _i64, _i64, _i64p, _i64p, _i64p, _vp, _vp]),
     "fi_kv_write": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64,
                                    _i64, _i64, _i64, _i64, _i64p, _i64p, _i64p, _i64p, _i64p,
                                    _vp, _vp]),

@@ -209,3 +209,55 @@ def store_kv_decode(cache: KVCache, layer_idx: int, k: torch.Tensor, v: torch.Te
     for b in range(B):
         cache._ensure_blocks(b, blk + 1)
     cache.write_tokens(layer_idx, k[:, None], v[:, None], pos)
+
+
+def rope_and_store(cache: KVCache, layer_idx: int, qkv: torch.Tensor, num_q_heads: int,
+                   cos_table: torch.Tensor, sin_table: torch.Tensor, start_pos,
+                   q_out: torch.Tensor = None, k_out: torch.Tensor = None) -> torch.Tensor:
+    """Fused RoPE of q and k plus the KV slot write (one launch).
+
+    Equivalent to the reference's ``apply_rope`` (kernels/rope.py:26-44, cos/sin rows
+    cast to fp16 as model.py:74-75 does) followed by storing the rotated k and v at
+    positions start_pos[b] + t (model.py:162-201), bit for bit.
+
+    qkv: [B, S, (nq + 2*nkv) * D] fp16 projection output (q | k | v heads);
+    cos_table / sin_table: fp32 [max_pos, D]; start_pos: int or [B] int32 device tensor.
+    Returns rotated q [B, S, nq, D] (``q_out`` if given). If ``k_out`` ([B, S, nkv, D])
+    is given, the rotated k is also written there.
+    """
+    cache.sync_block_table()
+    if qkv.dim() != 3 or qkv.dtype != torch.float16 or qkv.device != cache.device:
+        raise ValueError("qkv must be [batch, seq, heads*head_dim] float16 on the cache device")
+    B, S, W = qkv.shape
+    D, nkv = cache.head_dim, cache.num_heads
+    if W != (num_q_heads + 2 * nkv) * D:
+        raise ValueError(f"qkv width {W} != (nq + 2*nkv) * head_dim = {(num_q_heads + 2 * nkv) * D}")
+    if B > cache.block_table.shape[0]:
+        raise ValueError("batch larger than the block table; call _grow_batch first")
+    for name, t in (("cos_table", cos_table), ("sin_table", sin_table)):
+        if t.dtype != torch.float32 or t.device != cache.device or t.dim() != 2 or t.stride(1) != 1:
+            raise ValueError(f"{name} must be a float32 [max_pos, head_dim] table on the device")
+    if q_out is None:
+        q_out = torch.empty(B, S, num_q_heads, D, dtype=torch.float16, device=cache.device)
+    if isinstance(start_pos, torch.Tensor):
+        sp, sp_scalar = start_pos.to(torch.int32).contiguous(), 0
+    else:
+        sp, sp_scalar = None, int(start_pos)
+    kc, vc = cache.k[layer_idx], cache.v[layer_idx]
+    lib = _lib.load()
+    with with_device(cache.device):
+        err = error_word(cache.device)
+        st = lib.fi_rope_kv_write(
+            qkv.data_ptr(), B, S, num_q_heads, nkv, D, _lib.strides(*qkv.stride()),
+            cos_table.data_ptr(), sin_table.data_ptr(), cos_table.shape[0], cos_table.stride(0),
+            sp.data_ptr() if sp is not None else None, sp_scalar,
+            q_out.data_ptr(), _lib.strides(*q_out.stride()),
+            k_out.data_ptr() if k_out is not None else None,
+            _lib.strides(*k_out.stride()) if k_out is not None else None,
+            kc.data_ptr(), vc.data_ptr(), cache.block_table.data_ptr(), cache.num_blocks,
+            cache.block_size, cache.max_blocks_per_seq, _lib.strides(*kc.stride()),
+            _lib.strides(*vc.stride()), _lib.strides(*cache.block_table.stride()),
+            err.data_ptr() if err is not None else None, stream_of(cache.device))
+        _lib.check(st, "rope_and_store")
+        device_errors(err, "rope_and_store")
+    return q_out

@@ -18,10 +18,11 @@ input of token t+1 (there is no embedding or sampler in an attention-only stack)
 Weights are random N(0, 0.02) fp16 drawn on the device from a fixed seed, identical
 on every rank (same GPU model), then sliced to the rank's heads.
 
-The projections, RMSNorm and RoPE use PyTorch (cuBLAS GEMMs); they are outside
-the path this library implements. RMSNorm follows reference
-kernels/rms_norm.py:8-43 (fp32 math, fp16 out); RoPE follows kernels/rope.py:9-44
-(rotate-half form, tables for max_seq_len positions).
+The projections and RMSNorm use PyTorch (cuBLAS GEMMs; RMSNorm follows reference
+kernels/rms_norm.py:8-43, fp32 math, fp16 out); they are outside the path this
+library implements. RoPE (reference kernels/rope.py:9-44) and the KV slot write are
+one fused kernel (``rope_and_store`` / fi_rope_kv_write), bit-identical to the
+reference's fp16 ops. ``apply_rope`` below restates the reference's RoPE for tests.
 """
 
 from __future__ import annotations
@@ -32,7 +33,7 @@ import torch
 
 from fast_infer_b200._runtime import device_checks
 from fast_infer_b200.kernels.attention import flash_attention, paged_attention
-from fast_infer_b200.kv_cache import KVCache, store_kv_decode, store_kv_prefill
+from fast_infer_b200.kv_cache import KVCache, rope_and_store
 from fast_infer_b200.shard import HeadShard, gather_heads, head_shard
 
 
@@ -108,27 +109,27 @@ class AttentionStack:
         return o if self.world == 1 else self.gather(o)
 
     # ------------------------------------------------------------------ prefill
-    def _layer_qkv(self, w, h, cos, sin):
-        B, S, _ = h.shape
-        D, nq, nkv = self.D, self.shard.num_q_heads, self.shard.num_kv_heads
-        x = rms_norm(h, w["norm"], self.eps)
-        q, k, v = (x @ w["wqkv"]).split([nq * D, nkv * D, nkv * D], dim=-1)
-        q = apply_rope(q.view(B, S, nq, D), cos, sin)
-        k = apply_rope(k.view(B, S, nkv, D), cos, sin)
-        return q, k, v.view(B, S, nkv, D)
+    def _qkv(self, w, h):
+        return rms_norm(h, w["norm"], self.eps) @ w["wqkv"]
 
     def prefill(self, h: torch.Tensor) -> torch.Tensor:
-        """Prompt pass (reference model.py:67-69, 108-117): h [B, S, hidden] fp16."""
+        """Prompt pass (reference model.py:67-69, 101-117): h [B, S, hidden] fp16.
+        Per layer: projection, then one fused RoPE + KV slot-write launch, then the
+        causal prefill kernel on rotated q / k and the v columns of the projection."""
         B, S, _ = h.shape
         self.reset()
-        pos = torch.arange(S, device=self.device)
-        cos, sin = self.cos[pos].half(), self.sin[pos].half()
-        nq = self.shard.num_q_heads
+        D, nq, nkv = self.D, self.shard.num_q_heads, self.shard.num_kv_heads
+        need = (S + 63) // 64
+        for b in range(B):  # model.py:172-174 allocation order
+            self.cache._ensure_blocks(b, need)
+        self.cache.num_tokens = S
+        k_rot = torch.empty(B, S, nkv, D, dtype=torch.float16, device=self.device)
         for li, w in enumerate(self.layers):
-            q, k, v = self._layer_qkv(w, h, cos, sin)
-            o = flash_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2))
-            store_kv_prefill(self.cache, li, k, v)
-            o = self._gather(o.transpose(1, 2).reshape(B, S, nq * self.D))
+            qkv = self._qkv(w, h)
+            q_rot = rope_and_store(self.cache, li, qkv, nq, self.cos, self.sin, 0, k_out=k_rot)
+            v = qkv[..., (nq + nkv) * D:].view(B, S, nkv, D)
+            o = flash_attention(q_rot.transpose(1, 2), k_rot.transpose(1, 2), v.transpose(1, 2))
+            o = self._gather(o.transpose(1, 2).reshape(B, S, nq * D))
             h = h + o @ w["wo"]
         self.token_count = S
         return h
@@ -136,11 +137,10 @@ class AttentionStack:
     # ------------------------------------------------------------------- decode
     def _decode_state(self):
         """Device-resident step state, so one decode step is a fixed sequence of
-        launches (CUDA-graph capturable): position of the new token, per-sequence
-        context lengths (including it) and write positions."""
-        if getattr(self, "_dev_pos", None) is None:
+        launches (CUDA-graph capturable): per-sequence context lengths (including the
+        new token) and the new token's write / rotary position."""
+        if getattr(self, "_dev_ctx", None) is None:
             B = self.batch
-            self._dev_pos = torch.zeros(1, dtype=torch.int64, device=self.device)
             self._dev_ctx = torch.zeros(B, dtype=torch.int32, device=self.device)
             self._dev_start = torch.zeros(B, dtype=torch.int32, device=self.device)
             span = self.cache.max_blocks_per_seq * 64
@@ -155,20 +155,17 @@ class AttentionStack:
         """One decode token through every layer, reading positions from device
         memory (reference model.py:70-72, 118-131); advances them at the end."""
         B = self.batch
-        pos = self._dev_pos
-        cos, sin = self.cos.index_select(0, pos).half(), self.sin.index_select(0, pos).half()
         nq, D = self.shard.num_q_heads, self.D
         span = self.cache.max_blocks_per_seq * 64
         h = self._h_in
         for li, w in enumerate(self.layers):
-            q, k, v = self._layer_qkv(w, h, cos, sin)
-            self.cache.write_tokens(li, k, v, self._dev_start)
+            q = rope_and_store(self.cache, li, self._qkv(w, h), nq, self.cos, self.sin,
+                               self._dev_start)
             o = paged_attention(q[:, 0], self.cache.k[li], self.cache.v[li],
                                 self.cache.block_table, 64, 0, context_lens=self._dev_ctx,
                                 max_context_len=span, workspace=self._ws)
             o = self._gather(o.reshape(B, 1, nq * D))
             h = h + o @ w["wo"]
-        self._dev_pos.add_(1)
         self._dev_ctx.add_(1)
         self._dev_start.add_(1)
         self._h_in.copy_(h)
@@ -191,7 +188,6 @@ class AttentionStack:
         """Set the decode state after ``prefill``: h_last [B, 1, hidden] is the first
         decode input; positions continue from the prompt length."""
         self._decode_state()
-        self._dev_pos.fill_(self.token_count)
         self._dev_ctx.fill_(self.token_count + 1)
         self._dev_start.fill_(self.token_count)
         self._h_in.copy_(h_last)
@@ -211,13 +207,13 @@ class AttentionStack:
     def _capture(self):
         # Save the state, run the body once eagerly (first-call set-up of every
         # kernel), restore the state, then capture one step.
-        saved = [t.clone() for t in (self._dev_pos, self._dev_ctx, self._dev_start, self._h_in)]
+        saved = [t.clone() for t in (self._dev_ctx, self._dev_start, self._h_in)]
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
             self._decode_body()
         torch.cuda.current_stream(self.device).wait_stream(s)
-        for t, v in zip((self._dev_pos, self._dev_ctx, self._dev_start, self._h_in), saved):
+        for t, v in zip((self._dev_ctx, self._dev_start, self._h_in), saved):
             t.copy_(v)
         g = torch.cuda.CUDAGraph()
         # reading the device error word synchronises, which a capture forbids
@@ -237,7 +233,7 @@ class AttentionStack:
         otherwise one decode token (eager). h: [B, S, hidden] fp16."""
         if h.shape[1] > 1 or self.token_count == 0:
             return self.prefill(h)
-        if getattr(self, "_dev_pos", None) is None or self._graph is None:
+        if getattr(self, "_dev_ctx", None) is None or self._graph is None:
             self.begin_decode(h)
         else:
             self._h_in.copy_(h)

@@ -159,6 +159,36 @@ int fi_kv_write(const void* k, const void* v, void* k_cache, void* v_cache,
                 const int64_t* kc_strides, const int64_t* vc_strides, const int64_t* bt_strides,
                 int32_t* error_flag, void* stream);
 
+/*
+ * Fused rotary embedding + KV-cache slot write, from the QKV projection output.
+ *
+ * Replaces: kernels/rope.py:26-44 `apply_rope(q, k, cos, sin)` as called at
+ * model.py:101 (cos/sin rows cast to fp16, model.py:74-75) plus the slot writes of
+ * model.py:162-201, in one launch.
+ *
+ * qkv       : [batch, seq, (nq + 2*nkv) * head_dim] fp16, heads in the order q | k | v
+ *             (qkv_strides: 3 entries, innermost 1) — the fused projection output.
+ * cos_table,
+ * sin_table : fp32 [table_rows, table_stride] rotary tables (kernels/rope.py:9-16);
+ *             token t of sequence b uses row start_pos[b] + t (or start_pos_scalar + t).
+ * q_out     : [batch, seq, nq, head_dim] fp16 rotated q (q_out_strides: 4 entries).
+ * k_out     : optional dense [batch, seq, nkv, head_dim] rotated k (NULL = cache only).
+ * Rotated k and unchanged v go to page block_table[b, p / block_size], row
+ * p % block_size of k_cache / v_cache (layouts as in fi_kv_write).
+ * Every product and sum is rounded to fp16 as PyTorch's fp16 ops do, so results are
+ * bit-identical to the reference's apply_rope followed by its copies.
+ */
+int fi_rope_kv_write(const void* qkv, int64_t batch, int64_t seq, int64_t num_q_heads,
+                     int64_t num_kv_heads, int64_t head_dim, const int64_t* qkv_strides,
+                     const float* cos_table, const float* sin_table, int64_t table_rows,
+                     int64_t table_stride, const int32_t* start_pos, int64_t start_pos_scalar,
+                     void* q_out, const int64_t* q_out_strides, void* k_out,
+                     const int64_t* k_out_strides, void* k_cache, void* v_cache,
+                     const int32_t* block_table, int64_t num_blocks, int64_t block_size,
+                     int64_t max_blocks_per_seq, const int64_t* kc_strides,
+                     const int64_t* vc_strides, const int64_t* bt_strides, int32_t* error_flag,
+                     void* stream);
+
 #ifdef __cplusplus
 }
 #endif

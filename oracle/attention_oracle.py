@@ -390,6 +390,31 @@ def slot_write(k_cache: np.ndarray, v_cache: np.ndarray, k: np.ndarray, v: np.nd
 
 
 # ---------------------------------------------------------------------------
+# Rotary embedding (the producer of the K written by the slot writes).
+# ---------------------------------------------------------------------------
+
+def rope_tables(head_dim: int, max_seq_len: int, theta: float = 500000.0):
+    """fp32 cos/sin tables [max_seq_len, head_dim], reference kernels/rope.py:9-16."""
+    freq = (1.0 / (np.float32(theta) ** (np.arange(0, head_dim, 2, dtype=np.float32)
+                                         / np.float32(head_dim)))).astype(np.float32)
+    ang = np.outer(np.arange(max_seq_len, dtype=np.float32), freq).astype(np.float32)
+    ang = np.concatenate([ang, ang], axis=-1)
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+def apply_rope_fp16(x: np.ndarray, cos16: np.ndarray, sin16: np.ndarray) -> np.ndarray:
+    """x * cos + rotate_half(x) * sin with fp16 tensors, every op rounded to fp16
+    (reference kernels/rope.py:19-44). x: [B, S, H, D] fp16; cos16/sin16: [S, D] fp16."""
+    d = x.shape[-1]
+    rot = np.concatenate([-x[..., d // 2:], x[..., : d // 2]], axis=-1)
+    c = cos16[None, :, None, :].astype(np.float32)
+    s = sin16[None, :, None, :].astype(np.float32)
+    a = (x.astype(np.float32) * c).astype(np.float16)
+    b = (rot.astype(np.float32) * s).astype(np.float16)
+    return (a.astype(np.float32) + b.astype(np.float32)).astype(np.float16)
+
+
+# ---------------------------------------------------------------------------
 # Error metrics used by every parity test (north_star tolerances).
 # ---------------------------------------------------------------------------
 

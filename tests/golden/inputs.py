@@ -74,3 +74,16 @@ def kv_write_inputs():
         pk=randn_f16(rng, (L, B, S, H, D)), pv=randn_f16(rng, (L, B, S, H, D)),
         dk=randn_f16(rng, (T, L, B, H, D)), dv=randn_f16(rng, (T, L, B, H, D)),
     )
+
+
+ROPE_PREFILL_POS = tuple(range(6))
+ROPE_DECODE_POS = 300
+
+
+def rope_inputs():
+    """q/k for the RoPE fixture: a 6-token prefill and one decode token (B2, 24/8 heads)."""
+    rng = np.random.default_rng(31)
+    return dict(
+        q=randn_f16(rng, (2, 6, 24, 128)), k=randn_f16(rng, (2, 6, 8, 128)),
+        dq=randn_f16(rng, (2, 1, 24, 128)), dk=randn_f16(rng, (2, 1, 8, 128)),
+    )

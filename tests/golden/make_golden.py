@@ -18,6 +18,9 @@ Fixtures:
                         block-boundary cases, one reference call per sequence.
 * ``kv_write.npz``      block tables + pool digests after the reference model's
                         own ``_store_kv_prefill`` / ``_store_kv_decode``.
+* ``rope.npz``          the reference's ``apply_rope`` (kernels/rope.py) on a 6-token
+                        prefill and a decode token at position 300, with the fp16
+                        cos/sin rows model.py:74-75 feeds it.
 """
 
 from __future__ import annotations
@@ -35,8 +38,8 @@ HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parent.parent))
 
 from tests.golden.inputs import (  # noqa: E402
-    DECODE_RAGGED_LENS, KV_WRITE, PREFILL_SMALL_S, c1_inputs, decode_ragged_inputs,
-    kv_write_inputs, prefill_small_inputs)
+    DECODE_RAGGED_LENS, KV_WRITE, PREFILL_SMALL_S, ROPE_DECODE_POS, ROPE_PREFILL_POS, c1_inputs,
+    decode_ragged_inputs, kv_write_inputs, prefill_small_inputs, rope_inputs)
 
 
 def _import_reference(ref_path: str):
@@ -46,9 +49,10 @@ def _import_reference(ref_path: str):
     sys.path.insert(0, tmp)
     import torch  # noqa: F401
     from fast_infer.kernels import attention as ref_attn  # type: ignore
+    from fast_infer.kernels import rope as ref_rope  # type: ignore
     from fast_infer import kv_cache as ref_kv  # type: ignore
     from fast_infer import model as ref_model  # type: ignore
-    return ref_attn, ref_kv, ref_model
+    return ref_attn, ref_kv, ref_model, ref_rope
 
 
 def digest(a: np.ndarray) -> str:
@@ -59,7 +63,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
     args = ap.parse_args()
-    ref_attn, ref_kv, ref_model = _import_reference(args.reference)
+    ref_attn, ref_kv, ref_model, ref_rope = _import_reference(args.reference)
     import torch
     T = torch.from_numpy
 
@@ -139,6 +143,19 @@ def main():
         free_blocks=np.array(stub.kv_cache.free_blocks, np.int64),
         k_sha=digest(stub.kv_cache.k.numpy()), v_sha=digest(stub.kv_cache.v.numpy()),
     )
+    # ---- RoPE (producer of every K the slot writes store) --------------------
+    r = rope_inputs()
+    cos, sin = ref_rope.precompute_freqs(128, 4096, 500000.0, torch.device("cpu"))
+    pos = torch.tensor(ROPE_PREFILL_POS)
+    c16, s16 = cos[pos].to(torch.float16), sin[pos].to(torch.float16)
+    qr, kr = ref_rope.apply_rope(T(r["q"]), T(r["k"]), c16, s16)
+    dpos = torch.tensor([ROPE_DECODE_POS])
+    dc16, ds16 = cos[dpos].to(torch.float16), sin[dpos].to(torch.float16)
+    dqr, dkr = ref_rope.apply_rope(T(r["dq"]), T(r["dk"]), dc16, ds16)
+    np.savez_compressed(HERE / "rope.npz", cos16=c16.numpy(), sin16=s16.numpy(),
+                        dcos16=dc16.numpy(), dsin16=ds16.numpy(), q_rot=qr.numpy(),
+                        k_rot=kr.numpy(), dq_rot=dqr.numpy(), dk_rot=dkr.numpy(),
+                        cos_fp32_row300=cos[ROPE_DECODE_POS].numpy())
     print("golden fixtures written to", HERE)
 
 

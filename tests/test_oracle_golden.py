@@ -128,3 +128,17 @@ def test_kv_cache_out_of_memory_and_reset():
         cache.alloc_block(0)
     cache.reset()
     assert cache.free_blocks == [0, 1] and (cache.block_table == -1).all()
+
+
+def test_rope_oracle_bit_identical_to_reference():
+    from oracle.attention_oracle import apply_rope_fp16, rope_tables
+    from tests.golden.inputs import ROPE_DECODE_POS, rope_inputs
+    g = np.load(GOLDEN / "rope.npz")
+    r = rope_inputs()
+    assert np.array_equal(apply_rope_fp16(r["q"], g["cos16"], g["sin16"]), g["q_rot"])
+    assert np.array_equal(apply_rope_fp16(r["k"], g["cos16"], g["sin16"]), g["k_rot"])
+    assert np.array_equal(apply_rope_fp16(r["dq"], g["dcos16"], g["dsin16"]), g["dq_rot"])
+    assert np.array_equal(apply_rope_fp16(r["dk"], g["dcos16"], g["dsin16"]), g["dk_rot"])
+    cos, _ = rope_tables(128, 4096)
+    # fp32 cos of arguments up to ~300 rad: implementations differ by ~1e-5
+    assert np.allclose(cos[ROPE_DECODE_POS], g["cos_fp32_row300"], atol=1e-4)
