@@ -40,6 +40,9 @@ DECODE_LAYERS = 16
 C3_SEQS, C3_LO, C3_HI, C3_SEED = 64, 512, 4096, 2
 PF_B, PF_S, PF_SEED = 4, 2048, 1
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM bytes (read + write) per paged_decode_kernel launch on this workload's shape,
+# from `ncu --set full` (profiles/paged_decode_kernel_config5.md): 2.7375 GB + 8.9 MB.
+DECODE_TRAFFIC_NCU = 2.7375e9 + 8.925e6
 
 
 def load_peaks():
@@ -314,7 +317,8 @@ def run_ours(args):
             "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
             "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
             "peak_source": f"{peak_kind} hbm_gbs",
-            "traffic": None,
+            "traffic": DECODE_TRAFFIC_NCU,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch",
         },
         "prefill": {
             "workload": "config 2: causal prefill B4 x S2048, GQA 24/8 (K/V not expanded), D128",
