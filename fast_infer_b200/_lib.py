@@ -44,6 +44,9 @@ SIGNATURES = {
     "fi_last_error": (ctypes.c_char_p, []),
     "fi_prefill_fwd": (ctypes.c_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
                                       _i64p, _i64p, _i64p, _i64p, _f32, _vp, _vp]),
+    "fi_prefill_fwd_varlen": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
+                                             _i64, _i64, _i64p, _i64p, _i64p, _i64p, _f32, _vp,
+                                             _vp]),
     "fi_paged_decode_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64, _i64]),
     "fi_paged_decode": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                                        _i64, _i64, _i64, _i64, _i64, _i64p, _i64p, _i64p,

@@ -90,6 +90,7 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(uint32_t a_mn_major, uint3
 
 struct PrefillParams {
   int batch, hq, hk, group, seq_len, npairs, units;
+  const int32_t* cu_seqlens;  // packed (varlen) layout: sequence b = tokens [cu[b], cu[b+1])
   float scale_log2;
   __half* o;
   int64_t os[4];
@@ -108,6 +109,7 @@ struct PfBarriers {
 // One work unit = 256 consecutive query rows (two 128-row tiles) of one head.
 struct PfUnit {
   int b, h, hk, pair;
+  int start, len;  // first token of the sequence in the packed layout (0 if not packed), length
   int n[2];  // KV tiles each Q tile needs (0 = tile beyond seq_len)
   int nkv;   // KV tiles the unit streams = max(n[0], n[1])
 };
@@ -128,14 +130,33 @@ __device__ __forceinline__ PfUnit pf_unit(const PrefillParams& p, int k) {
   u.b = rem / p.hq;
   u.h = rem % p.hq;
   u.hk = u.h / p.group;
+  if (p.cu_seqlens) {
+    u.start = p.cu_seqlens[u.b];
+    u.len = p.cu_seqlens[u.b + 1] - u.start;
+  } else {
+    u.start = 0;
+    u.len = p.seq_len;
+  }
   for (int t = 0; t < 2; ++t) {
     const int r0 = u.pair * 2 * kBM + t * kBM;
-    u.n[t] = r0 < p.seq_len ? r0 / kBN + 1 : 0;
+    u.n[t] = r0 < u.len ? r0 / kBN + 1 : 0;
   }
   u.nkv = u.n[1] > 0 ? u.n[1] : u.n[0];
   return u;
 }
 
+// Loads one 64-column half of a 128-row tile: (batch, head, row) coordinates for
+// [B, H, S, D] tensors, (head, packed token) coordinates for packed [T, H, D] ones.
+template <bool kPacked>
+__device__ __forceinline__ void tma_tile_half(void* dst, const CUtensorMap* m, uint64_t* bar,
+                                              int d0, int row, int h, const PfUnit& u) {
+  if (kPacked)
+    tma_load_3d(dst, m, bar, d0, h, u.start + row);
+  else
+    tma_load_4d(dst, m, bar, d0, row, h, u.b);
+}
+
+template <bool kPacked>
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k,
@@ -195,14 +216,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const int k = pf_unit_index(r, cta, G);
         if (k >= p.units) break;
         const PfUnit u = pf_unit(p, k);
+        if (u.pair == p.npairs - 1 && u.h == 0 && (u.len < 0 || u.len > p.npairs * 2 * kBM))
+          set_error(p.err, FI_DEVERR_CONTEXT_LEN);  // cu_seqlens beyond max_seqlen
+        if (u.nkv == 0) continue;  // ragged batch: this sequence is shorter
         for (int t = 0; t < 2 && ok; ++t) {
           if (u.n[t] == 0) continue;
           if (qc[t] > 0) ok = mbar_wait(&bars->q_empty[t], (qc[t] - 1) & 1, p.err);
           if (!ok) break;
           const int r0 = u.pair * 2 * kBM + t * kBM;
           mbar_arrive_expect_tx(&bars->q_full[t], kTileBytes);
-          tma_load_4d(sQ + t * kTileBytes, &tm_q, &bars->q_full[t], 0, r0, u.h, u.b);
-          tma_load_4d(sQ + t * kTileBytes + kHalfBytes, &tm_q, &bars->q_full[t], 64, r0, u.h, u.b);
+          tma_tile_half<kPacked>(sQ + t * kTileBytes, &tm_q, &bars->q_full[t], 0, r0, u.h, u);
+          tma_tile_half<kPacked>(sQ + t * kTileBytes + kHalfBytes, &tm_q, &bars->q_full[t], 64,
+                                 r0, u.h, u);
           ++qc[t];
         }
         for (int j = 0; ok && j < u.nkv; ++j, ++g) {
@@ -210,12 +235,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           const uint32_t par = ((g / kPfStages) - 1) & 1;
           if (g >= kPfStages && !(ok = mbar_wait(&bars->k_empty[s], par, p.err))) break;
           mbar_arrive_expect_tx(&bars->k_full[s], kTileBytes);
-          tma_load_4d(sK + s * kTileBytes, &tm_k, &bars->k_full[s], 0, j * kBN, u.hk, u.b);
-          tma_load_4d(sK + s * kTileBytes + kHalfBytes, &tm_k, &bars->k_full[s], 64, j * kBN, u.hk, u.b);
+          tma_tile_half<kPacked>(sK + s * kTileBytes, &tm_k, &bars->k_full[s], 0, j * kBN, u.hk, u);
+          tma_tile_half<kPacked>(sK + s * kTileBytes + kHalfBytes, &tm_k, &bars->k_full[s], 64,
+                                 j * kBN, u.hk, u);
           if (g >= kPfStages && !(ok = mbar_wait(&bars->v_empty[s], par, p.err))) break;
           mbar_arrive_expect_tx(&bars->v_full[s], kTileBytes);
-          tma_load_4d(sV + s * kTileBytes, &tm_v, &bars->v_full[s], 0, j * kBN, u.hk, u.b);
-          tma_load_4d(sV + s * kTileBytes + kHalfBytes, &tm_v, &bars->v_full[s], 64, j * kBN, u.hk, u.b);
+          tma_tile_half<kPacked>(sV + s * kTileBytes, &tm_v, &bars->v_full[s], 0, j * kBN, u.hk, u);
+          tma_tile_half<kPacked>(sV + s * kTileBytes + kHalfBytes, &tm_v, &bars->v_full[s], 64,
+                                 j * kBN, u.hk, u);
         }
       }
     } else if (warp == 9 && lane == 0) {
@@ -251,6 +278,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const int k = pf_unit_index(r, cta, G);
         if (k >= p.units) break;
         const PfUnit u = pf_unit(p, k);
+        if (u.nkv == 0) continue;
         // First K tile of the unit, then S_t(0) for each live tile.
         ok = mbar_wait(&bars->k_full[g % kPfStages], (g / kPfStages) & 1, p.err);
         for (int t = 0; t < 2 && ok; ++t) {
@@ -437,9 +465,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (lane == 0) mbar_arrive(&bars->o_empty[t]);
       ++uc;
       const int grow = u.pair * 2 * kBM + t * kBM + row;
-      if (grow < p.seq_len) {
+      if (grow < u.len) {
         const float inv = l > 0.f ? 1.f / l : 0.f;
-        __half* orow = p.o + u.b * p.os[0] + u.h * p.os[1] + (int64_t)grow * p.os[2];
+        __half* orow = kPacked ? p.o + (int64_t)(u.start + grow) * p.os[0] + u.h * p.os[1]
+                               : p.o + u.b * p.os[0] + u.h * p.os[1] + (int64_t)grow * p.os[2];
 #pragma unroll
         for (int c8 = 0; c8 < kHD; c8 += 8) {
           uint4 pk;
@@ -479,6 +508,64 @@ static int make_bhsd_map(CUtensorMap* m, const void* base, int64_t B, int64_t H,
                       CU_TENSOR_MAP_SWIZZLE_128B, what);
 }
 
+// 3-D tensor map over a packed [T, H, 128] fp16 tensor with element strides st[3]
+// (token, head, d). Box: 64 columns x 1 head x 128 tokens, 128B swizzle.
+static int make_thd_map(CUtensorMap* m, const void* base, int64_t T, int64_t H,
+                        const int64_t* st, const char* what) {
+  if (st[2] != 1) return fail(FI_ERR_ALIGNMENT, "%s: innermost stride must be 1", what);
+  uint64_t dims[3] = {(uint64_t)kHD, (uint64_t)H, (uint64_t)T};
+  uint64_t sb[2] = {(uint64_t)st[1] * 2, (uint64_t)st[0] * 2};
+  if (H == 1) sb[0] = (uint64_t)kHD * 2;
+  const uint32_t box[3] = {64, 1, (uint32_t)kBM};
+  return encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, base, dims, sb, box,
+                      CU_TENSOR_MAP_SWIZZLE_128B, what);
+}
+
+static bool o_layout_ok(const void* o, const int64_t* os, int n) {
+  if (os[n - 1] != 1 || (reinterpret_cast<uintptr_t>(o) & 15) != 0) return false;
+  for (int i = 0; i + 1 < n; ++i)
+    if (os[i] % 8 != 0) return false;
+  return true;
+}
+
+template <bool kPacked>
+static int launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                          PrefillParams& p, int64_t batch, int64_t num_q_heads, void* stream) {
+  const int64_t units = (int64_t)p.npairs * batch * num_q_heads;
+  if (units > 0x7fffffff) return fail(FI_ERR_UNSUPPORTED, "fi_prefill_fwd: too many work units");
+  p.units = (int)units;
+  const int grid = (int)(units < sm_count() ? units : sm_count());
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(prefill_fwd_kernel<kPacked>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmemBytes);
+    if (e != cudaSuccess) return cuda_fail(e, "fi_prefill_fwd: cudaFuncSetAttribute");
+    attr_done[dev] = true;
+  }
+  prefill_fwd_kernel<kPacked><<<(unsigned)grid, kPfThreads, kPfSmemBytes,
+                                static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "fi_prefill_fwd: launch");
+  return FI_OK;
+}
+
+static void fill_common(PrefillParams& p, int64_t batch, int64_t hq, int64_t hk, int64_t max_len,
+                        float sm_scale, void* o, const int64_t* os, int nos, int32_t* err) {
+  p.batch = (int)batch;
+  p.hq = (int)hq;
+  p.hk = (int)hk;
+  p.group = (int)(hq / hk);
+  p.seq_len = (int)max_len;
+  p.npairs = (int)((max_len + 2 * kBM - 1) / (2 * kBM));
+  p.scale_log2 = (float)((double)sm_scale * 1.4426950408889634);
+  p.err = err;
+  p.o = static_cast<__half*>(o);
+  for (int i = 0; i < 4; ++i) p.os[i] = i < nos ? os[i] : 0;
+  p.cu_seqlens = nullptr;
+}
+
 }  // namespace fi
 
 extern "C" int fi_prefill_fwd(const void* q, const void* k, const void* v, void* o,
@@ -507,40 +594,51 @@ extern "C" int fi_prefill_fwd(const void* q, const void* k, const void* v, void*
   if (r != FI_OK) return r;
   r = make_bhsd_map(&tv, v, batch, num_kv_heads, seq_len, v_strides, "fi_prefill_fwd v");
   if (r != FI_OK) return r;
-  if (o_strides[3] != 1 || (reinterpret_cast<uintptr_t>(o) & 15) != 0 || o_strides[0] % 8 != 0 ||
-      o_strides[1] % 8 != 0 || o_strides[2] % 8 != 0)
+  if (!o_layout_ok(o, o_strides, 4))
     return fail(FI_ERR_ALIGNMENT,
                 "fi_prefill_fwd o: needs a 16-byte aligned base, unit innermost stride and "
                 "other strides multiple of 8");
-
   PrefillParams p;
-  p.batch = (int)batch;
-  p.hq = (int)num_q_heads;
-  p.hk = (int)num_kv_heads;
-  p.group = (int)(num_q_heads / num_kv_heads);
-  p.seq_len = (int)seq_len;
-  p.npairs = (int)((seq_len + 2 * kBM - 1) / (2 * kBM));
-  p.scale_log2 = (float)((double)sm_scale * 1.4426950408889634);
-  p.err = error_flag;
-  p.o = static_cast<__half*>(o);
-  for (int i = 0; i < 4; ++i) p.os[i] = o_strides[i];
-  const int64_t units = (int64_t)p.npairs * batch * num_q_heads;
-  if (units > 0x7fffffff) return fail(FI_ERR_UNSUPPORTED, "fi_prefill_fwd: too many work units");
-  p.units = (int)units;
-  const int grid = (int)(units < sm_count() ? units : sm_count());
+  fill_common(p, batch, num_q_heads, num_kv_heads, seq_len, sm_scale, o, o_strides, 4, error_flag);
+  return launch_prefill<false>(tq, tk, tv, p, batch, num_q_heads, stream);
+}
 
-  static bool attr_done[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(prefill_fwd_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmemBytes);
-    if (e != cudaSuccess) return cuda_fail(e, "fi_prefill_fwd: cudaFuncSetAttribute");
-    attr_done[dev] = true;
-  }
-  prefill_fwd_kernel<<<(unsigned)grid, kPfThreads, kPfSmemBytes,
-                       static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "fi_prefill_fwd: launch");
-  return FI_OK;
+extern "C" int fi_prefill_fwd_varlen(const void* q, const void* k, const void* v, void* o,
+                                     const int32_t* cu_seqlens, int64_t batch,
+                                     int64_t num_q_heads, int64_t num_kv_heads,
+                                     int64_t max_seqlen, int64_t total_tokens, int64_t head_dim,
+                                     const int64_t* q_strides, const int64_t* k_strides,
+                                     const int64_t* v_strides, const int64_t* o_strides,
+                                     float sm_scale, int32_t* error_flag, void* stream) {
+  using namespace fi;
+  clear_error();
+  if (batch < 0 || max_seqlen < 0 || total_tokens < 0 || num_q_heads <= 0 || num_kv_heads <= 0)
+    return fail(FI_ERR_INVALID_ARG, "fi_prefill_fwd_varlen: bad sizes");
+  if (head_dim != kHD)
+    return fail(FI_ERR_UNSUPPORTED, "fi_prefill_fwd_varlen: head_dim %lld != 128",
+                (long long)head_dim);
+  if (num_q_heads % num_kv_heads != 0)
+    return fail(FI_ERR_INVALID_ARG, "fi_prefill_fwd_varlen: num_q_heads %% num_kv_heads != 0");
+  if (batch == 0 || max_seqlen == 0 || total_tokens == 0) return FI_OK;
+  if (!q || !k || !v || !o || !cu_seqlens || !q_strides || !k_strides || !v_strides || !o_strides)
+    return fail(FI_ERR_INVALID_ARG, "fi_prefill_fwd_varlen: null pointer argument");
+  if (max_seqlen > (1 << 30) || total_tokens > (1ll << 31) || batch > 65535 ||
+      num_q_heads > 65535)
+    return fail(FI_ERR_UNSUPPORTED, "fi_prefill_fwd_varlen: sizes too large");
+  CUtensorMap tq, tk, tv;
+  int r = make_thd_map(&tq, q, total_tokens, num_q_heads, q_strides, "fi_prefill_fwd_varlen q");
+  if (r != FI_OK) return r;
+  r = make_thd_map(&tk, k, total_tokens, num_kv_heads, k_strides, "fi_prefill_fwd_varlen k");
+  if (r != FI_OK) return r;
+  r = make_thd_map(&tv, v, total_tokens, num_kv_heads, v_strides, "fi_prefill_fwd_varlen v");
+  if (r != FI_OK) return r;
+  if (!o_layout_ok(o, o_strides, 3))
+    return fail(FI_ERR_ALIGNMENT,
+                "fi_prefill_fwd_varlen o: needs a 16-byte aligned base, unit innermost stride "
+                "and other strides multiple of 8");
+  PrefillParams p;
+  fill_common(p, batch, num_q_heads, num_kv_heads, max_seqlen, sm_scale, o, o_strides, 3,
+              error_flag);
+  p.cu_seqlens = cu_seqlens;
+  return launch_prefill<true>(tq, tk, tv, p, batch, num_q_heads, stream);
 }

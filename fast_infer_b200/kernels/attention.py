@@ -91,6 +91,55 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return o
 
 
+def flash_attention_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                           cu_seqlens: torch.Tensor, max_seqlen: int,
+                           sm_scale: float = None) -> torch.Tensor:
+    """Causal prefill over a ragged batch packed along the token axis (extension; the
+    reference's ``flash_attention`` takes one shared sequence length).
+
+    q: [total_tokens, num_heads, 128] fp16; k, v: [total_tokens, num_kv_heads, 128];
+    sequence b owns tokens [cu_seqlens[b], cu_seqlens[b+1]) (int32 on the device);
+    max_seqlen (host int) bounds the lengths. Returns o shaped like q.
+    """
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _check_cuda_f16(name, t)
+        if t.dim() != 3 or t.shape[-1] != HEAD_DIM:
+            raise ValueError(f"{name} must be [total_tokens, heads, {HEAD_DIM}]")
+    total, num_heads, head_dim = q.shape
+    if k.shape != v.shape or k.shape[0] != total:
+        raise ValueError("k/v must be [total_tokens, num_kv_heads, head_dim] like q")
+    num_kv_heads = k.shape[1]
+    if num_heads % num_kv_heads != 0:
+        raise ValueError(f"num_heads {num_heads} not a multiple of k/v heads {num_kv_heads}")
+    if cu_seqlens.dim() != 1 or cu_seqlens.device != q.device:
+        raise ValueError("cu_seqlens must be a 1-D int32 tensor on q's device")
+    cu = cu_seqlens.to(torch.int32).contiguous()
+    batch = cu.numel() - 1
+    if sm_scale is None:
+        sm_scale = head_dim ** -0.5
+    o = torch.empty_like(q)
+    if batch <= 0 or total == 0:
+        return o
+    qx = q if _tma_ready(q) else q.contiguous()
+    kx = k if _tma_ready(k) else k.contiguous()
+    vx = v if _tma_ready(v) else v.contiguous()
+    ox = o if _tma_ready(o) else torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    lib = _lib.load()
+    with with_device(q.device):
+        err = error_word(q.device)
+        st = lib.fi_prefill_fwd_varlen(
+            qx.data_ptr(), kx.data_ptr(), vx.data_ptr(), ox.data_ptr(), cu.data_ptr(), batch,
+            num_heads, num_kv_heads, int(max_seqlen), total, head_dim,
+            _lib.strides(*qx.stride()), _lib.strides(*kx.stride()),
+            _lib.strides(*vx.stride()), _lib.strides(*ox.stride()), float(sm_scale),
+            err.data_ptr() if err is not None else None, stream_of(q.device))
+        _lib.check(st, "flash_attention_varlen")
+        device_errors(err, "flash_attention_varlen")
+    if ox is not o:
+        o.copy_(ox)
+    return o
+
+
 def paged_attention_workspace_bytes(batch: int, num_q_heads: int, num_kv_heads: int,
                                     max_context_len: int, pages_per_split: int = 0) -> int:
     """Split-KV workspace bytes ``paged_attention`` needs for these sizes."""

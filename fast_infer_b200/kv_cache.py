@@ -54,6 +54,9 @@ class KVCache:
         self.free_blocks = list(range(self.num_blocks))
         self._allocated = 0
         self.num_tokens = 0
+        # Extension: per-sequence stored-token counts (the reference keeps only the
+        # batch-wide num_tokens, kv_cache.py:39 / model.py:59,67-72).
+        self.seq_lens = np.zeros(1, np.int64)
 
     # ------------------------------------------------------------ allocation
     def _grow_batch(self, batch_size: int):
@@ -63,6 +66,9 @@ class KVCache:
         nt = np.full((batch_size, self.max_blocks_per_seq), -1, np.int32)
         nt[: self._bt.shape[0]] = self._bt
         self._bt = nt
+        sl = np.zeros(batch_size, np.int64)
+        sl[: self.seq_lens.shape[0]] = self.seq_lens
+        self.seq_lens = sl
         self.block_table = torch.from_numpy(nt.copy()).to(self.device)
         self._dirty = False
 
@@ -118,6 +124,12 @@ class KVCache:
         self.free_blocks = list(range(self.num_blocks))
         self._allocated = 0
         self.num_tokens = 0
+        self.seq_lens[:] = 0
+
+    def context_lens(self, batch: int = None) -> torch.Tensor:
+        """Per-sequence token counts as a device int32 tensor (for paged_attention)."""
+        n = self.seq_lens.shape[0] if batch is None else batch
+        return torch.from_numpy(self.seq_lens[:n].astype(np.int32)).to(self.device)
 
     # ------------------------------------------------------------ slot writes
     def write_tokens(self, layer_idx: int, k: torch.Tensor, v: torch.Tensor,
@@ -209,6 +221,32 @@ def store_kv_decode(cache: KVCache, layer_idx: int, k: torch.Tensor, v: torch.Te
     for b in range(B):
         cache._ensure_blocks(b, blk + 1)
     cache.write_tokens(layer_idx, k[:, None], v[:, None], pos)
+
+
+def store_kv_ragged(cache: KVCache, layer_idx: int, k: torch.Tensor, v: torch.Tensor,
+                    start_pos, n_new):
+    """Per-sequence slot write (extension for ragged batches).
+
+    k, v: [B, T, H, D] (rows past n_new[b] are padding); token t of sequence b is
+    stored at position start_pos[b] + t for t < n_new[b]. Blocks are allocated on
+    demand per sequence in batch order (the reference's first-free-slot / FIFO rule),
+    and at layer 0 ``cache.seq_lens`` grows to cover the written positions.
+    """
+    start = np.asarray(start_pos, np.int64).reshape(-1)
+    nn = np.asarray(n_new, np.int64).reshape(-1)
+    B = k.shape[0]
+    if start.shape[0] != B or nn.shape[0] != B:
+        raise ValueError("start_pos and n_new need one entry per sequence")
+    cache._grow_batch(B)
+    bs = cache.block_size
+    for b in range(B):
+        if nn[b] > 0:
+            cache._ensure_blocks(b, int((start[b] + nn[b] + bs - 1) // bs))
+    if layer_idx == 0:
+        cache.seq_lens[:B] = np.maximum(cache.seq_lens[:B], start + nn)
+    dev = cache.device
+    cache.write_tokens(layer_idx, k, v, torch.from_numpy(start.astype(np.int32)).to(dev),
+                       torch.from_numpy(nn.astype(np.int32)).to(dev))
 
 
 def rope_and_store(cache: KVCache, layer_idx: int, qkv: torch.Tensor, num_q_heads: int,

@@ -68,6 +68,24 @@ int fi_prefill_fwd(const void* q, const void* k, const void* v, void* o, int64_t
                    const int64_t* o_strides, float sm_scale, int32_t* error_flag, void* stream);
 
 /*
+ * Causal prefill over a ragged batch packed along the token axis (no counterpart
+ * in the reference, whose flash_attention takes one shared length; the per-sequence
+ * state it lacks is noted at model.py:59,67-72 and kv_cache.py:39).
+ *
+ * q, o : [total_tokens, num_q_heads, 128] fp16 (strides: 3 entries, token/head/dim);
+ * k, v : [total_tokens, num_kv_heads, 128] fp16; sequence b owns tokens
+ *        [cu_seqlens[b], cu_seqlens[b+1]) (device int32 [batch + 1], non-decreasing).
+ * max_seqlen bounds every length (longer sequences set FI_DEVERR_CONTEXT_LEN and are
+ * only partly computed). Same arithmetic and GQA rule as fi_prefill_fwd.
+ */
+int fi_prefill_fwd_varlen(const void* q, const void* k, const void* v, void* o,
+                          const int32_t* cu_seqlens, int64_t batch, int64_t num_q_heads,
+                          int64_t num_kv_heads, int64_t max_seqlen, int64_t total_tokens,
+                          int64_t head_dim, const int64_t* q_strides, const int64_t* k_strides,
+                          const int64_t* v_strides, const int64_t* o_strides, float sm_scale,
+                          int32_t* error_flag, void* stream);
+
+/*
  * Bytes of split-KV workspace fi_paged_decode needs for these sizes
  * (pages_per_split = 0 selects the library's automatic split size).
  */

@@ -127,3 +127,39 @@ def test_config2_full_size(cuda_device):
     assert max_abs <= MAX_ABS_TOL and rel <= REL_L2_TOL, (max_abs, rel)
     for _ in range(3):  # deterministic: identical bytes run to run
         assert torch.equal(flash_attention(q, k, v), out)
+
+
+@pytest.mark.parametrize("lens", [(1, 77, 128, 129, 300, 512, 0, 1000), (2048, 5, 700)])
+def test_varlen_ragged_batch_vs_fp32(cuda_device, device_checks, lens):
+    """Packed ragged batch (extension): every sequence equals its own causal attention."""
+    from fast_infer_b200.kernels.attention import flash_attention_varlen
+    torch.manual_seed(len(lens))
+    T = sum(lens)
+    q = torch.randn(T, 24, 128, device=cuda_device).half()
+    k = torch.randn(T, 8, 128, device=cuda_device).half()
+    v = torch.randn(T, 8, 128, device=cuda_device).half()
+    cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device=cuda_device)
+    out = flash_attention_varlen(q, k, v, cu, max(lens))
+    for b, n in enumerate(lens):
+        if n == 0:
+            continue
+        s0 = int(cu[b])
+        qs = q[s0:s0 + n].transpose(0, 1)[None]
+        ks = k[s0:s0 + n].transpose(0, 1)[None]
+        vs = v[s0:s0 + n].transpose(0, 1)[None]
+        ref = torch_causal_fp32(qs, ks, vs)[0].transpose(0, 1)
+        _ok(out[s0:s0 + n].float().cpu().numpy(), ref.cpu().numpy(), f"seq {b} len {n}")
+
+
+def test_varlen_equal_lengths_match_uniform_kernel(cuda_device, device_checks):
+    from fast_infer_b200.kernels.attention import flash_attention, flash_attention_varlen
+    torch.manual_seed(5)
+    B, S = 3, 333
+    q = torch.randn(B, S, 24, 128, device=cuda_device).half()
+    k = torch.randn(B, S, 8, 128, device=cuda_device).half()
+    v = torch.randn(B, S, 8, 128, device=cuda_device).half()
+    cu = torch.arange(0, (B + 1) * S, S, dtype=torch.int32, device=cuda_device)
+    o_var = flash_attention_varlen(q.reshape(B * S, 24, 128), k.reshape(B * S, 8, 128),
+                                   v.reshape(B * S, 8, 128), cu, S)
+    o_uni = flash_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2))
+    assert torch.equal(o_var.reshape(B, S, 24, 128), o_uni.transpose(1, 2))
