@@ -34,7 +34,10 @@ constexpr int kD = 128;
 constexpr int kPage = 64;
 constexpr int kDecWarps = 4;
 constexpr int kDecThreads = (kDecWarps + 1) * 32;
-constexpr int kDecStages = 3;
+#ifndef FI_DEC_STAGES
+#define FI_DEC_STAGES 3
+#endif
+constexpr int kDecStages = FI_DEC_STAGES;
 constexpr int kRegionBytes = kPage * 64 * 2;    // 64 rows x 64 fp16
 constexpr int kStageBytes = 4 * kRegionBytes;   // K lo, K hi, V lo, V hi
 constexpr int kMaxPagesPerSplit = 32;

@@ -6,27 +6,32 @@
 // with hk = h / (Hq / Hk); fp16 in, fp32 softmax/accumulation, fp16 out.
 //
 // B200 design:
-// * A CTA owns 256 consecutive query rows of one head as two 128-row tiles (T0, T1)
-//   that share every K/V tile fetched; work units are issued longest-first so the
-//   causal triangle load-balances across the 148 SMs.
-// * Warp roles (320 threads): warps 0-3 = softmax/epilogue of T0, warps 4-7 = T1,
-//   warp 8 = TMA producer, warp 9 = UMMA issuer (one thread).
+// * Persistent kernel, one CTA per SM. A work unit is 256 consecutive query rows of
+//   one head as two 128-row tiles (T0, T1) that share every K/V tile fetched; units
+//   are numbered longest-first and dealt to CTAs in snake order, so the causal
+//   triangle load-balances across the 148 SMs. Barrier phases carry across units,
+//   so the next unit's K/V and Q loads and first S MMA overlap this unit's tail.
+// * Warp roles (384 threads): warps 0-3 = softmax/epilogue of T0, warps 4-7 = T1,
+//   warp 8 = TMA producer, warp 9 = UMMA issuer (one thread), warps 10-11 only give
+//   their registers to the softmax warpgroups (setmaxnreg 184 / 136).
 // * Tensor memory (512 columns): S0 | S1 | O0 | O1, 128 fp32 columns each.
 //   S_t = Q_t K^T is a 128x128x128 tcgen05.mma (A, B from 128B-swizzled shared
 //   memory, K-major). Softmax threads own one row each (TMEM lane = row), read S
 //   with tcgen05.ld, write P as packed fp16 over the first 64 columns of S_t, and
 //   the PV product O_t += P V reads P straight from tensor memory (A operand in
-//   TMEM, V as an MN-major shared-memory operand). No S/P round trip through
-//   shared memory or registers of other warps.
+//   TMEM, V as an MN-major shared-memory operand).
 // * Online softmax in base 2 with a lazy rescale: O_t and l are rescaled only when
 //   a row's running max grows by more than 8 (2^8 headroom in fp16 P), which after
 //   the first tiles almost never happens. The result is exact either way because
-//   numerator and denominator use the same stale max.
+//   numerator and denominator use the same stale max. A share of the exponentials
+//   runs as a polynomial on the FMA pipe (exp2_poly_x2) next to MUFU.
 // * The MMA issue order S0(j), S1(j), PV0(j), S0(j+1), PV1(j), S1(j+1), ... lets
 //   the tensor core work on one tile while the other tile's softmax runs.
-// * Epilogue: O/l -> fp16 into the (now idle) Q tile's shared memory in the same
-//   swizzled layout, then one TMA store per 64-column half (rows past seq_len are
-//   clipped by the tensor map).
+// * Epilogue: O_t is read from TMEM (then released for the next unit), divided by
+//   l, and each thread stores its fp16 row straight to global memory.
+// * Packed variable-length batches (fi_prefill_fwd_varlen) run the same kernel with
+//   3-D TMA maps over [tokens, H, D] and per-sequence lengths from cu_seqlens.
+
 #include <math.h>
 
 #include "common.cuh"
@@ -219,17 +224,22 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         if (u.pair == p.npairs - 1 && u.h == 0 && (u.len < 0 || u.len > p.npairs * 2 * kBM))
           set_error(p.err, FI_DEVERR_CONTEXT_LEN);  // cu_seqlens beyond max_seqlen
         if (u.nkv == 0) continue;  // ragged batch: this sequence is shorter
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (u.n[t] == 0) continue;
-          if (qc[t] > 0) ok = mbar_wait(&bars->q_empty[t], (qc[t] - 1) & 1, p.err);
-          if (!ok) break;
-          const int r0 = u.pair * 2 * kBM + t * kBM;
-          mbar_arrive_expect_tx(&bars->q_full[t], kTileBytes);
-          tma_tile_half<kPacked>(sQ + t * kTileBytes, &tm_q, &bars->q_full[t], 0, r0, u.h, u);
-          tma_tile_half<kPacked>(sQ + t * kTileBytes + kHalfBytes, &tm_q, &bars->q_full[t], 64,
-                                 r0, u.h, u);
-          ++qc[t];
-        }
+        // K/V tile 0 of the unit goes out before the Q loads: its ring slot frees
+        // two steps before the previous unit ends, while the Q buffers only free
+        // after that unit's last S MMA.
+        auto load_q = [&]() {
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (u.n[t] == 0) continue;
+            if (qc[t] > 0) ok = mbar_wait(&bars->q_empty[t], (qc[t] - 1) & 1, p.err);
+            if (!ok) break;
+            const int r0 = u.pair * 2 * kBM + t * kBM;
+            mbar_arrive_expect_tx(&bars->q_full[t], kTileBytes);
+            tma_tile_half<kPacked>(sQ + t * kTileBytes, &tm_q, &bars->q_full[t], 0, r0, u.h, u);
+            tma_tile_half<kPacked>(sQ + t * kTileBytes + kHalfBytes, &tm_q, &bars->q_full[t], 64,
+                                   r0, u.h, u);
+            ++qc[t];
+          }
+        };
         for (int j = 0; ok && j < u.nkv; ++j, ++g) {
           const int s = g % kPfStages;
           const uint32_t par = ((g / kPfStages) - 1) & 1;
@@ -243,6 +253,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           tma_tile_half<kPacked>(sV + s * kTileBytes, &tm_v, &bars->v_full[s], 0, j * kBN, u.hk, u);
           tma_tile_half<kPacked>(sV + s * kTileBytes + kHalfBytes, &tm_v, &bars->v_full[s], 64,
                                  j * kBN, u.hk, u);
+          if (j == 0) load_q();
         }
       }
     } else if (warp == 9 && lane == 0) {
