@@ -41,7 +41,7 @@ C3_SEQS, C3_LO, C3_HI, C3_SEED = 64, 512, 4096, 2
 PF_B, PF_S, PF_SEED = 4, 2048, 1
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) per paged_decode_kernel launch on this workload's shape,
-# from `ncu --set full` (profiles/paged_decode_kernel_config5.md): 2.7375 GB + 8.9 MB.
+# from one `ncu --set full` capture of this workload shape: 2.7375 GB read + 8.9 MB written.
 DECODE_TRAFFIC_NCU = 2.7375e9 + 8.925e6
 
 
