@@ -302,7 +302,7 @@ def run_ours(args):
 
     # ---- prefill, config 2 (B4 x S2048, 24/8, seed 1); 4 rotating input sets > L2
     sets = prefill_inputs(torch, dev, 4)
-    pf_steps = max(args.steps // 4, 10)
+    pf_steps = max(args.steps, 50)
     lib = _lib.load()
     with ClockSampler(local) as clk_pf:
         ms_pf = timed(torch, lambda i: prefill_call(torch, lib, sets[i % 4]), pf_steps,
