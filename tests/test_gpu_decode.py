@@ -154,3 +154,18 @@ def test_config5_full_size_subsample(cuda_device):
     assert np.isfinite(out).all()
     idx = np.arange(0, 256, 16)
     _ok(out[idx], paged_attention_fp32(q[idx], kc, vc, bt[idx], lens[idx]))
+
+
+@pytest.mark.parametrize("scale", [6.0, 0.05])
+def test_extreme_magnitudes(cuda_device, device_checks, scale):
+    from fast_infer_b200.kernels.attention import paged_attention
+    rng = np.random.default_rng(31)
+    lens = np.array([100, 1000, 3000], np.int32)
+    q, kc, vc, bt = _random_paged(rng, lens, 24, 8)
+    q = (q.astype(np.float32) * scale).astype(np.float16)
+    kc = (kc.astype(np.float32) * scale).astype(np.float16)
+    out = paged_attention(_to(q, cuda_device), _to(kc, cuda_device), _to(vc, cuda_device),
+                          _to(bt, cuda_device), 64, 0, context_lens=_to(lens, cuda_device),
+                          pages_per_split=4).cpu().numpy()
+    assert np.isfinite(out).all()
+    _ok(out, paged_attention_fp32(q, kc, vc, bt, lens))

@@ -163,3 +163,36 @@ def test_varlen_equal_lengths_match_uniform_kernel(cuda_device, device_checks):
                                    v.reshape(B * S, 8, 128), cu, S)
     o_uni = flash_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2))
     assert torch.equal(o_var.reshape(B, S, 24, 128), o_uni.transpose(1, 2))
+
+
+@pytest.mark.parametrize("scale", [6.0, 0.05])
+def test_extreme_magnitudes_vs_fp32(cuda_device, device_checks, scale):
+    """Peaky softmax (large scores: many lazy-rescale events, one dominant key) and
+    nearly uniform softmax (tiny scores) both stay within tolerance."""
+    from fast_infer_b200.kernels.attention import flash_attention
+    torch.manual_seed(11)
+    q = (torch.randn(2, 6, 700, 128, device=cuda_device) * scale).half()
+    k = (torch.randn(2, 2, 700, 128, device=cuda_device) * scale).half()
+    v = torch.randn(2, 2, 700, 128, device=cuda_device).half()
+    out = flash_attention(q, k, v)
+    assert torch.isfinite(out).all()
+    # The north_star bound (2e-3 / 1e-3) is specified for N(0,1) inputs. With scores
+    # 36x larger the softmax is nearly one-hot over V values up to ~4, and rounding P
+    # to fp16 (as every FlashAttention PV product does) alone reaches ~2e-3 absolute;
+    # the bound here is 4e-3 absolute and the north_star relative-L2.
+    max_abs, rel = error_stats(out.float().cpu().numpy(), torch_causal_fp32(q, k, v).cpu().numpy())
+    assert max_abs <= 4e-3 and rel <= REL_L2_TOL, (scale, max_abs, rel)
+
+
+def test_increasing_scores_force_rescales(cuda_device, device_checks):
+    """Keys whose scores grow along the sequence make the running max rise at every
+    KV tile, so the O/l rescale path runs on every step."""
+    from fast_infer_b200.kernels.attention import flash_attention
+    torch.manual_seed(12)
+    S = 1024
+    q = torch.ones(1, 2, S, 128, device=cuda_device).half() * 0.5
+    ramp = torch.linspace(0, 4, S, device=cuda_device)[:, None]
+    k = (torch.randn(1, 2, S, 128, device=cuda_device) * 0.1 + ramp).half()
+    v = torch.randn(1, 2, S, 128, device=cuda_device).half()
+    out = flash_attention(q, k, v)
+    _ok(out.float().cpu().numpy(), torch_causal_fp32(q, k, v).cpu().numpy())
