@@ -87,3 +87,27 @@ def rope_inputs():
         q=randn_f16(rng, (2, 6, 24, 128)), k=randn_f16(rng, (2, 6, 8, 128)),
         dq=randn_f16(rng, (2, 1, 24, 128)), dk=randn_f16(rng, (2, 1, 8, 128)),
     )
+
+
+# INT4 dequant-matmul fixture: (name, N, K, groupsize, M values).
+INT4_CASES = (
+    ("a", 192, 384, 128, (1, 5, 16, 33)),
+    ("b", 100, 256, 128, (3,)),
+    ("g64", 64, 256, 64, (2,)),
+)
+
+
+def int4_inputs(name: str):
+    """Weights N(0, 0.02) and activations N(0, 1), fp16, for one INT4_CASES entry.
+
+    Case "a" plants an all-zero quantization group (scale clamp) and one outlier.
+    """
+    case = {c[0]: c for c in INT4_CASES}[name]
+    _, n, k, g, ms = case
+    rng = np.random.default_rng(41 + n + k)
+    w = (rng.standard_normal(size=(n, k), dtype=np.float32) * 0.02).astype(np.float16)
+    if name == "a":
+        w[0, :g] = 0
+        w[1, 3] = np.float16(5.0)
+    xs = {m: randn_f16(rng, (m, k)) for m in ms}
+    return w, xs, g

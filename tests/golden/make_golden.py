@@ -21,6 +21,10 @@ Fixtures:
 * ``rope.npz``          the reference's ``apply_rope`` (kernels/rope.py) on a 6-token
                         prefill and a decode token at position 300, with the fp16
                         cos/sin rows model.py:74-75 feeds it.
+* ``int4.npz``          the reference's ``quantize_int4_groupwise`` and
+                        ``dequantize_int4`` (loader.py), ``_dequant_storage`` and the
+                        fused ``int4_matmul`` Triton kernel (kernels/matmul.py) on the
+                        ``INT4_CASES`` shapes (ragged N, groupsize 64, a clamped group).
 """
 
 from __future__ import annotations
@@ -38,8 +42,9 @@ HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parent.parent))
 
 from tests.golden.inputs import (  # noqa: E402
-    DECODE_RAGGED_LENS, KV_WRITE, PREFILL_SMALL_S, ROPE_DECODE_POS, ROPE_PREFILL_POS, c1_inputs,
-    decode_ragged_inputs, kv_write_inputs, prefill_small_inputs, rope_inputs)
+    DECODE_RAGGED_LENS, INT4_CASES, KV_WRITE, PREFILL_SMALL_S, ROPE_DECODE_POS, ROPE_PREFILL_POS,
+    c1_inputs, decode_ragged_inputs, int4_inputs, kv_write_inputs, prefill_small_inputs,
+    rope_inputs)
 
 
 def _import_reference(ref_path: str):
@@ -55,6 +60,12 @@ def _import_reference(ref_path: str):
     return ref_attn, ref_kv, ref_model, ref_rope
 
 
+def _import_reference_int4():
+    from fast_infer import loader as ref_loader  # type: ignore
+    from fast_infer.kernels import matmul as ref_matmul  # type: ignore
+    return ref_loader, ref_matmul
+
+
 def digest(a: np.ndarray) -> str:
     return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
 
@@ -62,10 +73,20 @@ def digest(a: np.ndarray) -> str:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
+    ap.add_argument("--only", choices=["attention", "int4"], default=None,
+                    help="regenerate one group of fixtures (default: all)")
     args = ap.parse_args()
     ref_attn, ref_kv, ref_model, ref_rope = _import_reference(args.reference)
     import torch
     T = torch.from_numpy
+    if args.only != "int4":
+        _attention_fixtures(ref_attn, ref_kv, ref_model, ref_rope, torch, T)
+    if args.only != "attention":
+        _int4_fixtures(T)
+    print("golden fixtures written to", HERE)
+
+
+def _attention_fixtures(ref_attn, ref_kv, ref_model, ref_rope, torch, T):
 
     # ---- config 1 -------------------------------------------------------
     c1 = c1_inputs()
@@ -156,7 +177,23 @@ def main():
                         dcos16=dc16.numpy(), dsin16=ds16.numpy(), q_rot=qr.numpy(),
                         k_rot=kr.numpy(), dq_rot=dqr.numpy(), dk_rot=dkr.numpy(),
                         cos_fp32_row300=cos[ROPE_DECODE_POS].numpy())
-    print("golden fixtures written to", HERE)
+
+
+def _int4_fixtures(T):
+    """INT4 group-wise weights and the fused dequant-matmul."""
+    ref_loader, ref_matmul = _import_reference_int4()
+    out = {}
+    for name, n, k, g, ms in INT4_CASES:
+        w, xs, g = int4_inputs(name)
+        packed, scales = ref_loader.quantize_int4_groupwise(T(w), groupsize=g)
+        out[f"{name}_packed"] = packed.numpy()
+        out[f"{name}_scales"] = scales.numpy()
+        out[f"{name}_dequant"] = ref_loader.dequantize_int4(packed, scales, groupsize=g).numpy()
+        out[f"{name}_dequant_storage"] = ref_matmul._dequant_storage(packed, scales, g).numpy()
+        for m, x in xs.items():
+            out[f"{name}_c_m{m}"] = ref_matmul.int4_matmul(T(x), (packed, scales),
+                                                           groupsize=g).numpy()
+    np.savez_compressed(HERE / "int4.npz", **out)
 
 
 if __name__ == "__main__":
