@@ -207,6 +207,70 @@ int fi_rope_kv_write(const void* qkv, int64_t batch, int64_t seq, int64_t num_q_
                      const int64_t* vc_strides, const int64_t* bt_strides, int32_t* error_flag,
                      void* stream);
 
+/* ---- INT4 group-wise weights (the projections around attention) ---------- */
+
+/*
+ * Weight format of every INT4 entry point (reference loader.py:9-41,
+ * `quantize_int4_groupwise`): packed int8 [N, K/2], byte j of row n holds w[n, 2j] in
+ * its low nibble and w[n, 2j+1] in its high nibble (two's complement, [-8, 7]);
+ * scales fp16 [N, K/groupsize]; weight value fp16(q * scale). K % groupsize == 0.
+ */
+
+/* Bytes of split-K workspace fi_int4_gemm needs for these sizes (0 = none). */
+size_t fi_int4_gemm_workspace_size(int64_t m, int64_t n, int64_t k, int64_t groupsize);
+
+/*
+ * C[M, N] = x[M, K] @ dequant(W)^T, fp16 in / fp16 out, fp32 accumulation, for
+ * decode-sized M (1..64; larger M returns FI_ERR_UNSUPPORTED — dequantize with
+ * fi_int4_dequant and use a dense GEMM).
+ *
+ * Replaces: kernels/matmul.py:14-132 `_fused_int4_matmul` (reached through
+ * `int4_matmul(x, (packed, scales), groupsize)`, kernels/matmul.py:217-231, from
+ * model.py:91-93,134 and kernels/mlp.py:49,52 in the default memory mode).
+ *
+ * x       : [M, K] fp16, x_strides {row, 1}; 16-byte aligned base, row stride a
+ *           multiple of 8.
+ * packed  : [N, K/2] int8, packed_strides {row bytes, 1}; 16-byte aligned base and
+ *           row stride.
+ * scales  : [N, K/groupsize] fp16, any strides. groupsize a multiple of 32.
+ * c       : [M, N] fp16, any strides.
+ * workspace: caller-owned device buffer of fi_int4_gemm_workspace_size(...) bytes,
+ *           256-byte aligned. Its first 256 KB hold split-K counters that must be
+ *           ZERO before the first use; every call leaves them zero again, so one
+ *           workspace serves calls of any shape. Calls sharing a workspace must be
+ *           ordered on one stream. N is limited to 65536 * 128.
+ * Deterministic: split-K partial sums are added in a fixed order.
+ */
+int fi_int4_gemm(const void* x, const void* packed, const void* scales, void* c, int64_t m,
+                 int64_t n, int64_t k, int64_t groupsize, const int64_t* x_strides,
+                 const int64_t* packed_strides, const int64_t* scales_strides,
+                 const int64_t* c_strides, void* workspace, size_t workspace_bytes,
+                 void* stream);
+
+/*
+ * Dequantize INT4 weights to fp16 [N, K] (out_strides {row, 1}; 16-byte aligned base,
+ * row stride a multiple of 8), bit-identical to the reference.
+ *
+ * Replaces: kernels/matmul.py:309-326 `_dequant_storage` and loader.py:157-190
+ * `dequantize_int4` (the speed-mode weight preparation, kernels/matmul.py:236-266).
+ * packed: 4-byte aligned base and row stride; groupsize a multiple of 8.
+ */
+int fi_int4_dequant(const void* packed, const void* scales, void* out, int64_t n, int64_t k,
+                    int64_t groupsize, const int64_t* packed_strides,
+                    const int64_t* scales_strides, const int64_t* out_strides, void* stream);
+
+/*
+ * Quantize fp16 weights w [N, K] (w_strides: 2 entries, any) to the INT4 format
+ * above, bit-identical to the reference: per group, scale = fp16(max(max|w|,
+ * fp16(1e-6)) / 7), q = round-half-even(fp16(w / scale)) clamped to [-8, 7].
+ *
+ * Replaces: loader.py:9-41 `quantize_int4_groupwise` (run once per linear weight at
+ * load time, loader.py:150-154). packed_strides {row bytes, 1}; groupsize even.
+ */
+int fi_int4_quantize(const void* w, void* packed, void* scales, int64_t n, int64_t k,
+                     int64_t groupsize, const int64_t* w_strides, const int64_t* packed_strides,
+                     const int64_t* scales_strides, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
