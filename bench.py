@@ -14,9 +14,11 @@ partitioning, no collective on the data path): weak scaling.
 Headline ``value``: algorithmic HBM GB/s of the whole job (K/V bytes once + Q/O +
 block-table entries, summed over ranks, / max-over-ranks device time).
 Extra measurements on the same JSON line: the causal prefill of config 2
-(B4 x S2048, TFLOP/s) and decode on the config-3 shape, each against the
-measured roofline in MEASURED_PEAKS.json; ``e2e`` through the public API with
-pinned host buffers; ``cpu_baseline`` = the CPU oracle on a bounded sample.
+(B4 x S2048, TFLOP/s), decode on the config-3 shape, and the INT4 group-wise
+dequant-matmul of the Llama-3.2-3B layer projections at decode batch sizes (weight
+GB/s), each against the measured roofline in MEASURED_PEAKS.json; ``e2e`` through
+the public API with pinned host buffers; ``cpu_baseline`` = the CPU oracle on a
+bounded sample.
 """
 
 from __future__ import annotations
@@ -43,6 +45,10 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # DRAM bytes (read + write) per paged_decode_kernel launch on this workload's shape,
 # from one `ncu --set full` capture of this workload shape: 2.7375 GB read + 8.9 MB written.
 DECODE_TRAFFIC_NCU = 2.7375e9 + 8.925e6
+# INT4 projections of one Llama-3.2-3B layer: (name, N = out features, K = in features).
+INT4_SHAPES = (("qkv", 5120, 3072), ("o", 3072, 3072), ("gate_up", 16384, 3072),
+               ("down", 3072, 8192))
+INT4_LAYERS, INT4_GROUP, INT4_SEED = 8, 128, 6
 
 
 def load_peaks():
@@ -317,6 +323,8 @@ def run_ours(args):
     c3_gbs = wl3.bytes / (ms3 * 1e-3) / 1e9
 
     stack = run_stack(torch, dev, rank, world, dist) if not args.no_stack else None
+    int4 = run_int4(torch, dev, max(args.steps // 8, 20), args.warmup, hbm_peak,
+                    cpu=(rank == 0 and world == 1 and not args.no_cpu_baseline))
 
     launches_per_step = 2 + (1 if _needs_combine(wl) else 0)
     result = {
@@ -364,6 +372,7 @@ def run_ours(args):
             "frac": round(c3_gbs / hbm_peak, 4),
         },
         "stack": stack,
+        "int4_gemm": int4,
         "e2e": {
             "value": round(total_bytes / (e2e_step_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
             "ms_per_step": round(e2e_step_ms, 5),
@@ -417,6 +426,9 @@ def run_only(args):
     out = {"only": args.only, "steps": args.steps, "warmup": args.warmup}
     if args.only == "stack":
         out.update(run_stack(torch, dev, 0, 1, None))
+    elif args.only == "int4":
+        out.update(run_int4(torch, dev, args.steps, args.warmup, float(peaks["hbm_gbs"]),
+                            cpu=False))
     elif args.only == "prefill":
         sets = prefill_inputs(torch, dev, 4)
         ms = timed(torch, lambda i: prefill_call(torch, lib, sets[i % 4]), args.steps,
@@ -499,6 +511,76 @@ def run_stack(torch, dev, rank, world, dist, warmup=1):
         "cuda_graph": use_graph,
         "finite": finite,
     }
+
+
+def int4_weight_bytes(n, k):
+    """Bytes a dequant-matmul must read for one weight: nibbles + fp16 group scales."""
+    return n * k // 2 + n * (k // INT4_GROUP) * 2
+
+
+def run_int4(torch, dev, steps, warmup, hbm_peak, cpu=False, ms=(16, 1)):
+    """INT4 group-wise dequant-matmul (the reference's default memory-mode projections)
+    on the four projections of a Llama-3.2-3B layer, at decode batch M = 16 (config 4)
+    and M = 1. Eight layers of random N(0, 0.02) weights quantized on the GPU (440 MB,
+    larger than L2) are cycled; one step = all 4 x 8 projections, replayed from one
+    CUDA graph. Reports weight-stream GB/s against the HBM roofline."""
+    from fast_infer_b200.kernels.matmul import int4_matmul
+    from fast_infer_b200.loader import quantize_int4_groupwise
+    g = torch.Generator(device=dev)
+    g.manual_seed(INT4_SEED)
+    layers = [{name: quantize_int4_groupwise(
+        (torch.randn(n, k, device=dev, generator=g) * 0.02).half(), INT4_GROUP)
+        for name, n, k in INT4_SHAPES} for _ in range(INT4_LAYERS)]
+    wbytes = sum(int4_weight_bytes(n, k) for _, n, k in INT4_SHAPES)
+    out = {"workload": "Llama-3.2-3B layer projections qkv 5120x3072, o 3072x3072, gate_up "
+                       "16384x3072, down 3072x8192, INT4 groupsize 128, 8 layers rotated "
+                       "(weights > L2), one CUDA graph per step",
+           "weight_bytes_per_layer": wbytes}
+    for m in ms:
+        xs = {name: torch.randn(m, k, device=dev, generator=g).half() for name, _, k in INT4_SHAPES}
+
+        def body():
+            for w in layers:
+                for name, _, _ in INT4_SHAPES:
+                    int4_matmul(xs[name], w[name], groupsize=INT4_GROUP)
+
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            body()  # sizes the side stream's split-K workspace before capture
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
+                body()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        ms_step = timed(torch, lambda i: graph.replay(), steps, warmup) / steps
+        gbs = wbytes * INT4_LAYERS / (ms_step * 1e-3) / 1e9
+        out[f"m{m}"] = {"us_per_layer": round(ms_step * 1e3 / INT4_LAYERS, 2),
+                        "gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 4),
+                        "launches_per_layer": len(INT4_SHAPES)}
+        del graph
+    if cpu:
+        out["cpu_baseline"] = cpu_baseline_int4()
+    return out
+
+
+def cpu_baseline_int4(reps=3):
+    """The CPU oracle's dequant-matmul (numpy, one thread of BLAS) on the o projection
+    (3072 x 3072, M = 16): weight GB/s."""
+    from oracle.int4_oracle import int4_matmul, quantize_int4_groupwise
+    rng = np.random.default_rng(INT4_SEED)
+    n = k = 3072
+    w = (rng.standard_normal((n, k), dtype=np.float32) * 0.02).astype(np.float16)
+    packed, scales = quantize_int4_groupwise(w, INT4_GROUP)
+    x = rng.standard_normal((16, k), dtype=np.float32).astype(np.float16)
+    from threadpoolctl import threadpool_limits
+    best = float("inf")
+    with threadpool_limits(1):
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            int4_matmul(x, packed, scales, INT4_GROUP)
+            best = min(best, time.perf_counter() - t0)
+    return {"value": round(int4_weight_bytes(n, k) / best / 1e9, 3), "unit": "GB/s", "cores": 1,
+            "kind": "port", "sample": "oracle int4_matmul, o projection 3072x3072, M=16"}
 
 
 def _needs_combine(wl):
@@ -655,7 +737,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-stack", action="store_true", help="skip the config-4 stack section")
-    ap.add_argument("--only", choices=["decode", "decode_c3", "prefill", "stack"], default=None,
+    ap.add_argument("--only", choices=["decode", "decode_c3", "prefill", "stack", "int4"],
+                    default=None,
                     help="time one kernel family alone (profiling runs); prints one JSON line")
     ap.add_argument("--layers", type=int, default=DECODE_LAYERS,
                     help="resident KV-cache layers of the decode workload")

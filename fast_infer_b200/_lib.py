@@ -60,9 +60,8 @@ SIGNATURES = {
     "fi_kv_write": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64,
                                    _i64, _i64, _i64, _i64, _i64p, _i64p, _i64p, _i64p, _i64p,
                                    _vp, _vp]),
-    "fi_int4_gemm_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),
     "fi_int4_gemm": (ctypes.c_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64p, _i64p,
-                                    _i64p, _i64p, _vp, _sz, _vp]),
+                                    _i64p, _i64p, _vp, _vp]),
     "fi_int4_dequant": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64p, _i64p, _i64p,
                                        _vp]),
     "fi_int4_quantize": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64p, _i64p, _i64p,

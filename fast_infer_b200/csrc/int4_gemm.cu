@@ -1,52 +1,68 @@
-// INT4 group-wise dequant-matmul for decode-sized M, and the storage dequantizer.
+// INT4 group-wise dequant-matmul for decode-sized M, the storage dequantizer and the
+// quantizer.
 //
 // Replaces the reference's memory-mode projection path (model.py:15-21 default
-// memory_efficient=True; kernels/matmul.py:14-132 `_fused_int4_matmul`, and
-// kernels/matmul.py:309-326 `_dequant_storage` / loader.py:157-190
-// `dequantize_int4` for the dequantizer).
+// memory_efficient=True; kernels/matmul.py:14-132 `_fused_int4_matmul`), its
+// storage dequant (kernels/matmul.py:309-326 `_dequant_storage`, loader.py:157-190
+// `dequantize_int4`) and its quantizer (loader.py:9-41 `quantize_int4_groupwise`).
 //
 // Weight format (loader.py:9-41): packed int8 [N, K/2], byte j of row n holds
 // w[n, 2j] in its low nibble and w[n, 2j+1] in its high nibble, two's complement in
 // [-8, 7]; scales fp16 [N, K/groupsize]. A weight is fp16(q * scale) (one rounding),
 // exactly as the reference computes it; products and sums are fp32, output fp16.
 //
-// fi_int4_gemm (M <= 64) is bound by the weight bytes it streams from HBM:
-// * A CTA (8 warps) owns 128 weight rows (output columns) and one K slice of at most
-//   512. Each thread streams 16-byte chunks (32 nibbles) of two weight rows, all of
-//   its slice's loads in flight before any math.
-// * Nibbles become fp16 without a conversion instruction: lop3 places a nibble
-//   (sign bit flipped) in the mantissa of 1024.0 (0x6400), an exact HSUB2/HFMA2
-//   removes the offset, and HMUL2 by the group scale gives fp16(q * scale). One
-//   32-bit word yields the pairs (k0,k4) (k1,k5) (k2,k6) (k3,k7).
-// * mma.sync m16n8k16 multiplies: the k order inside each 8-group is permuted the
-//   same way for x (when x is staged into shared memory, once per CTA) and for the
-//   weights, so every fragment comes from one 16-byte shared load or one weight word.
-// * Split-K: partial sums (fp32, rows < M only) go to the caller's workspace; the
-//   CTA that finishes a column block last sums them in split order (deterministic)
-//   and writes fp16. Its per-column-block counter returns to zero for the next call.
+// fi_int4_gemm (M <= 64) streams the 4-bit weights once from HBM:
+// * Persistent CTAs, one producer warp + 8 consumer warps. The producer streams
+//   16-row x 512-byte weight tiles (1024 k) with TMA into a shared-memory ring (one
+//   3-D box of 4 x 128-byte chunks per tile, 128B-swizzled so the consumers' 16-byte
+//   reads are conflict-free); each consumer warp takes 128 k of every tile.
+// * Nibbles become fp16 without a conversion instruction: lop3 drops a nibble (sign
+//   bit flipped) into the mantissa of 1024.0 (0x6400) in each half of a register, an
+//   exact f16x2 subtract / fma removes the offset, and an f16x2 multiply by the group
+//   scale gives fp16(q * scale) with the reference's single rounding.
+// * mma.sync m16n8k16 computes C^T = W x^T: the 16 weight rows are the MMA's M, the
+//   tokens its N (tiles of 8), so a decode batch of up to 8 tokens costs two MMAs per
+//   32-bit weight word and no padding. The 8 warps' partial sums are added in warp
+//   order through shared memory (deterministic); no scratch memory is used.
 #include <cuda_fp16.h>
+
+#include <cstring>
 
 #include "common.cuh"
 #include "host_common.h"
 
 namespace fi {
 
-constexpr int kI4Threads = 256;  // 8 warps
-constexpr int kI4Cols = 128;     // weight rows (output columns) per CTA: 8 warps x 2 x 8
-constexpr int kI4KIter = 128;    // k per warp iteration: 4 threads x 32 nibbles
-constexpr int kI4MaxIters = 4;   // warp iterations per K slice
-constexpr int kI4MaxM = 64;      // four m16 tiles
-constexpr int kI4MaxCounters = 65536;  // split-K counters, one per column block: 256 KB
+constexpr int kI4Consumers = 8;                         // math warps
+constexpr int kI4Threads = (kI4Consumers + 1) * 32;     // + one TMA producer warp
+constexpr int kI4Rows = 16;        // weight rows (output columns) per work item
+constexpr int kI4KIter = 128;      // k per consumer warp per round: 4 threads x 32 nibbles
+constexpr int kI4RoundK = kI4Consumers * kI4KIter;      // 1024 k per round
+constexpr int kI4BoxBytes = 128;   // one 128B-swizzled TMA box: 16 rows x 128 packed bytes
+constexpr int kI4Boxes = kI4RoundK / 2 / kI4BoxBytes;   // 4 boxes per stage
+constexpr int kI4StageBytes = kI4Rows * kI4RoundK / 2;  // 8 KB
+#ifndef FI_I4_STAGES
+#define FI_I4_STAGES 6
+#endif
+constexpr int kI4Stages = FI_I4_STAGES;
+constexpr int kI4ScaleBytes = kI4Rows * (kI4RoundK / 128) * 2;  // 256: 16 rows x 8 fp16
+constexpr int kI4MaxM = 64;        // up to eight 8-token tiles
+constexpr int kI4ConsumerBar = 1;  // named barrier of the 256 consumer threads
 
 struct I4Args {
   const __half* x;
-  const uint8_t* w;
   const __half* s;
   __half* c;
-  float* partial;      // [splits, M, Npad] fp32 (splits > 1)
-  unsigned* counters;  // [gridDim.x]
-  int M, N, K, gs, ks, splits, npad;
-  int64_t xs0, ws0, ss0, ss1, cs0, cs1;
+  int* err;
+  int M, N, K, gs, gs_shift;  // gs_shift = log2(gs) for a power of two, else -1
+  int rounds, xstride;        // k rounds of 1024; staged x row stride (halves)
+  int tma3d;                  // 1: one 3-D box per stage (K % 256 == 0), 0: four 2-D boxes
+  int tma_scales;             // 1: each round's 16 x 8 scales arrive by TMA with its weights
+  int64_t xs0, ss0, ss1, cs0, cs1;
+};
+
+struct I4Bars {
+  uint64_t full[kI4Stages], empty[kI4Stages];
 };
 
 // (a & b) ^ c
@@ -56,167 +72,258 @@ __device__ __forceinline__ uint32_t lop3_and_xor(uint32_t a, uint32_t b, uint32_
   return d;
 }
 
-__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+// f16x2 arithmetic on raw 32-bit registers, round-to-nearest-even, no contraction.
+__device__ __forceinline__ uint32_t hfma2_rn(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ uint32_t hmul2_rn(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
 
 // One packed word (nibbles k0..k7, k0 lowest) -> fp16(q * scale) as the half2 pairs
-// (k0,k4) (k1,k5) (k2,k6) (k3,k7). All steps before the multiply are exact.
-__device__ __forceinline__ void dequant_word(uint32_t q, __half2 s2, uint32_t* p) {
-  const __half2 off_lo = __floats2half2_rn(1032.f, 1032.f);   // 1024 + 8
-  const __half2 sixteenth = __floats2half2_rn(0.0625f, 0.0625f);
-  const __half2 off_hi = __floats2half2_rn(-72.f, -72.f);     // (1024 + 16*8) / 16
-  const uint32_t q2 = q >> 8;
-  // low nibble of each half: 1024 + (u ^ 8); bits 4-7: 1024 + 16 * (u ^ 8)
-  const __half2 t0 = u2h(lop3_and_xor(q, 0x000F000Fu, 0x64086408u));
-  const __half2 t1 = u2h(lop3_and_xor(q, 0x00F000F0u, 0x64806480u));
-  const __half2 t2 = u2h(lop3_and_xor(q2, 0x000F000Fu, 0x64086408u));
-  const __half2 t3 = u2h(lop3_and_xor(q2, 0x00F000F0u, 0x64806480u));
-  p[0] = h2u(__hmul2(__hsub2(t0, off_lo), s2));
-  p[1] = h2u(__hmul2(__hfma2(t1, sixteenth, off_hi), s2));
-  p[2] = h2u(__hmul2(__hsub2(t2, off_lo), s2));
-  p[3] = h2u(__hmul2(__hfma2(t3, sixteenth, off_hi), s2));
-}
-
-__device__ __forceinline__ uint4 ldg_stream(const void* p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-
-// Shared-memory position (in 16-byte chunks) of chunk c of staged row r: rows are
-// padded by one chunk and bit 1 of the chunk index is flipped in odd 8-chunk blocks,
-// so the fragment loads of a warp (rows g, g+1 x chunks 4t + wd) never share banks.
-__device__ __forceinline__ int xs_pos(int r, int c, int row_chunks) {
-  return r * (row_chunks + 1) + (c ^ (((c >> 3) & 1) << 1));
-}
-
-template <int MT>
-__global__ void __launch_bounds__(kI4Threads) int4_gemm_kernel(const I4Args a) {
-  extern __shared__ uint4 xs[];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, t = lane & 3;
-  const int cb = blockIdx.x, split = blockIdx.y;
-  const int k0 = split * a.ks;
-  const int klen = min(a.ks, a.K - k0);  // > 0, multiple of 32
-  const int row_chunks = a.ks / 8;
-
-  // ---- stage x[0:16*MT, k0:k0+klen) with each 8-group in the order 0,4,1,5,2,6,3,7
-  for (int i = tid; i < MT * 16 * row_chunks; i += kI4Threads) {
-    const int r = i / row_chunks, c = i - r * row_chunks;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (r < a.M && c * 8 < klen) {
-      const uint4 u = *reinterpret_cast<const uint4*>(a.x + r * a.xs0 + k0 + c * 8);
-      v.x = __byte_perm(u.x, u.z, 0x5410);  // (h0, h4)
-      v.y = __byte_perm(u.x, u.z, 0x7632);  // (h1, h5)
-      v.z = __byte_perm(u.y, u.w, 0x5410);  // (h2, h6)
-      v.w = __byte_perm(u.y, u.w, 0x7632);  // (h3, h7)
-    }
-    xs[xs_pos(r, c, row_chunks)] = v;
-  }
-
-  // ---- stream this thread's weight chunks (rows na, nb; k = kb + 32t .. +32)
-  const int nbase = cb * kI4Cols + warp * 16;
-  const int na = nbase + g, nb = nbase + 8 + g;
-  const int nit = (klen + kI4KIter - 1) / kI4KIter;
-  uint4 wa[kI4MaxIters], wb[kI4MaxIters];
-  __half sa[kI4MaxIters], sb[kI4MaxIters];
+// (k0,k1) (k2,k3) (k4,k5) (k6,k7); s2 = the fp16 scale in both halves. Byte b is
+// copied to all four byte positions; the low half keeps bits 0-3 (value 1024 + u'),
+// the high half bits 4-7 of its byte (1024 + 16 u'), u' = u ^ 8;
+// h * (1, 1/16) - (1032, 72) = q exactly, then one rounding in the multiply by s2.
+__device__ __forceinline__ void dequant_word(uint32_t q, uint32_t s2, uint32_t* p) {
+  constexpr uint32_t kMul = 0x2C003C00u;  // (1.0, 0.0625)
+  constexpr uint32_t kOff = 0xD480E408u;  // (-1032.0, -72.0)
 #pragma unroll
-  for (int it = 0; it < kI4MaxIters; ++it) {
-    wa[it] = make_uint4(0u, 0u, 0u, 0u);
-    wb[it] = make_uint4(0u, 0u, 0u, 0u);
-    sa[it] = __float2half(0.f);
-    sb[it] = __float2half(0.f);
-    const int kk = it * kI4KIter + 32 * t;  // offset inside the slice
-    if (it < nit && kk < klen) {
-      const int kabs = k0 + kk;
-      const int grp = kabs / a.gs;
-      if (na < a.N) {
-        wa[it] = ldg_stream(a.w + na * a.ws0 + kabs / 2);
-        sa[it] = a.s[na * a.ss0 + grp * a.ss1];
-      }
-      if (nb < a.N) {
-        wb[it] = ldg_stream(a.w + nb * a.ws0 + kabs / 2);
-        sb[it] = a.s[nb * a.ss0 + grp * a.ss1];
-      }
+  for (int b = 0; b < 4; ++b) {
+    const uint32_t r = __byte_perm(q, 0u, 0x1111u * b);
+    p[b] = hmul2_rn(hfma2_rn(lop3_and_xor(r, 0x00F0000Fu, 0x64806408u), kMul, kOff), s2);
+  }
+}
+
+// Same values in the pair order (k0,k4) (k1,k5) (k2,k6) (k3,k7), three operations fewer:
+// each 16-bit half takes its nibble straight from the word (bits 0-3 -> 1024 + u',
+// bits 4-7 -> 1024 + 16 u'), the odd nibbles of each byte after one shift by 8.
+__device__ __forceinline__ void dequant_word_perm(uint32_t q, uint32_t s2, uint32_t* p) {
+  constexpr uint32_t kOffLo = 0x64086408u;  // (1032.0, 1032.0)
+  constexpr uint32_t kSixteenth = 0x2C002C00u;  // (0.0625, 0.0625)
+  constexpr uint32_t kOffHi = 0xD480D480u;  // (-72.0, -72.0)
+  const uint32_t q2 = q >> 8;
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(lop3_and_xor(q, 0x000F000Fu, 0x64086408u)), "r"(kOffLo));
+  p[0] = hmul2_rn(d, s2);
+  p[1] = hmul2_rn(hfma2_rn(lop3_and_xor(q, 0x00F000F0u, 0x64806480u), kSixteenth, kOffHi), s2);
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(lop3_and_xor(q2, 0x000F000Fu, 0x64086408u)), "r"(kOffLo));
+  p[2] = hmul2_rn(d, s2);
+  p[3] = hmul2_rn(hfma2_rn(lop3_and_xor(q2, 0x00F000F0u, 0x64806480u), kSixteenth, kOffHi), s2);
+}
+
+// fp16 bits in both halves of a 32-bit register
+__device__ __forceinline__ uint32_t splat16(uint16_t h) { return __byte_perm(h, 0u, 0x1010u); }
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, uint64_t* bar, int c0,
+                                            int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// Persistent: CTA b takes work items b, b + grid, ... ; an item = 16 weight rows x all
+// of K, processed in rounds of 1024 k. The producer warp streams each round's
+// 16 x 512-byte weight tile into a kI4Stages ring as [4 chunks][16 rows][128 bytes],
+// 128B-swizzled;
+// consumer warp w multiplies k = round*1024 + w*128 + 32t .. +32 of both 8-row halves
+// (rows g and g+8 of the tile) against x, computing C^T = W x^T with the weight rows
+// as the MMA's M dimension and the tokens as N (tiles of 8). At the end of an item the
+// 8 warps add their partial sums in warp order through shared memory.
+// kSmemX: x is staged once into shared memory (rows < M, each 8-group in the order
+// 0,4,1,5,2,6,3,7 that dequant_word_perm produces, zeros past K); otherwise x
+// fragments come from global memory in natural order and dequant_word is used.
+// Every mbarrier wait is bounded: after a timeout (FI_DEVERR_TIMEOUT) the waits are
+// skipped, the loops still run to the end and the producer lets its copies land.
+template <int NT, bool kSmemX>
+__global__ void __launch_bounds__(kI4Threads, 1)
+    int4_gemm_kernel(const __grid_constant__ CUtensorMap tm_w,
+                     const __grid_constant__ CUtensorMap tm_s, const I4Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  uint8_t* sstages = stages + kI4Stages * kI4StageBytes;  // kI4Stages x 256-byte scale tiles
+  I4Bars* bars = reinterpret_cast<I4Bars*>(sstages + kI4Stages * kI4ScaleBytes);
+  __half* xs = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(bars) + 256);
+  __shared__ float red[kI4Consumers][NT * 8][kI4Rows + 1];
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int items = (a.N + kI4Rows - 1) / kI4Rows;
+  const int my_items = blockIdx.x < items ? (items - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  const int total = my_items * a.rounds;
+
+  if (tid == 0) {
+    for (int i = 0; i < kI4Stages; ++i) {
+      mbar_init(&bars->full[i], 1);
+      mbar_init(&bars->empty[i], kI4Consumers * 32);
     }
+    fence_barrier_init();
   }
   __syncthreads();
 
-  float acc[MT][2][4];
+  if (warp == kI4Consumers) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tm_w);
+      if (a.tma_scales) prefetch_tmap(&tm_s);
+      bool dead = false;
+      for (int q = 0; q < total; ++q) {
+        const int st = q % kI4Stages;
+        if (q >= kI4Stages && !dead)
+          dead = !mbar_wait(&bars->empty[st], ((q / kI4Stages) - 1) & 1, a.err);
+        const int item = blockIdx.x + (q / a.rounds) * gridDim.x, r = q % a.rounds;
+        mbar_arrive_expect_tx(&bars->full[st],
+                              kI4StageBytes + (a.tma_scales ? kI4ScaleBytes : 0));
+        if (a.tma_scales)  // scales [N, K/128] fp16: 8 groups x 16 rows
+          tma_load_2d(sstages + st * kI4ScaleBytes, &tm_s, &bars->full[st],
+                      r * (kI4RoundK / 128), item * kI4Rows);
+        if (a.tma3d) {
+          // (byte, row, 128-byte chunk): one box = 4 chunks x 16 rows x 128 bytes
+          tma_load_3d(stages + st * kI4StageBytes, &tm_w, &bars->full[st], 0, item * kI4Rows,
+                      r * kI4Boxes);
+        } else {
 #pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[mt][j][e] = 0.f;
-
-#pragma unroll
-  for (int it = 0; it < kI4MaxIters; ++it) {
-    if (it >= nit) break;
-    const __half2 s2a = __half2half2(sa[it]), s2b = __half2half2(sb[it]);
-    const uint32_t qa[4] = {wa[it].x, wa[it].y, wa[it].z, wa[it].w};
-    const uint32_t qb[4] = {wb[it].x, wb[it].y, wb[it].z, wb[it].w};
-#pragma unroll
-    for (int wd = 0; wd < 4; ++wd) {
-      uint32_t ba[4], bb[4];
-      dequant_word(qa[wd], s2a, ba);
-      dequant_word(qb[wd], s2b, bb);
-      const int c = it * 16 + 4 * t + wd;
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        const uint4 u = xs[xs_pos(mt * 16 + g, c, row_chunks)];
-        const uint4 v = xs[xs_pos(mt * 16 + 8 + g, c, row_chunks)];
-        mma_16816(acc[mt][0], u.x, v.x, u.y, v.y, ba[0], ba[1]);
-        mma_16816(acc[mt][0], u.z, v.z, u.w, v.w, ba[2], ba[3]);
-        mma_16816(acc[mt][1], u.x, v.x, u.y, v.y, bb[0], bb[1]);
-        mma_16816(acc[mt][1], u.z, v.z, u.w, v.w, bb[2], bb[3]);
-      }
-    }
-  }
-
-  // ---- epilogue: C fragment rows g / g+8, columns 2t, 2t+1 of each 8-column block
-  if (a.splits == 1) {
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int m = mt * 16 + g + (e >> 1) * 8;
-          const int n = nbase + j * 8 + 2 * t + (e & 1);
-          if (m < a.M && n < a.N) a.c[m * a.cs0 + n * a.cs1] = __float2half_rn(acc[mt][j][e]);
+          for (int b = 0; b < kI4Boxes; ++b)
+            tma_load_2d(stages + st * kI4StageBytes + b * (kI4Rows * kI4BoxBytes), &tm_w,
+                        &bars->full[st], r * (kI4RoundK / 2) + b * kI4BoxBytes, item * kI4Rows);
         }
+      }
+      // Let the last copy of every stage land before the CTA can exit.
+      for (int q = total > kI4Stages ? total - kI4Stages : 0; q < total; ++q)
+        mbar_wait(&bars->full[q % kI4Stages], (q / kI4Stages) & 1, a.err);
+    }
     return;
   }
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int m = mt * 16 + g + h * 8;
-        const int n = nbase + j * 8 + 2 * t;  // < npad
-        if (m < a.M)
-          *reinterpret_cast<float2*>(a.partial + ((int64_t)split * a.M + m) * a.npad + n) =
-              make_float2(acc[mt][j][2 * h], acc[mt][j][2 * h + 1]);
+
+  // ---------------------------------------------------------------- consumers
+  const int g = lane >> 2, t = lane & 3;
+  if constexpr (kSmemX) {
+    const int chunks = a.rounds * (kI4RoundK / 8);
+    const int kchunks = a.K / 8;
+    for (int i = tid; i < a.M * chunks; i += kI4Consumers * 32) {
+      const int m = i / chunks, c = i - m * chunks;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (c < kchunks) {
+        const uint4 u = *reinterpret_cast<const uint4*>(a.x + m * a.xs0 + c * 8);
+        v = make_uint4(__byte_perm(u.x, u.z, 0x5410), __byte_perm(u.x, u.z, 0x7632),
+                       __byte_perm(u.y, u.w, 0x5410), __byte_perm(u.y, u.w, 0x7632));
       }
-  __threadfence();
-  __syncthreads();
-  __shared__ int s_last;
-  if (tid == 0) s_last = atomicAdd(&a.counters[cb], 1u) == (unsigned)(a.splits - 1);
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  for (int i = tid; i < a.M * kI4Cols; i += kI4Threads) {
-    const int m = i / kI4Cols, n = cb * kI4Cols + (i - m * kI4Cols);
-    float sum = 0.f;
-    for (int sp = 0; sp < a.splits; ++sp)
-      sum += __ldcg(a.partial + ((int64_t)sp * a.M + m) * a.npad + n);
-    if (n < a.N) a.c[m * a.cs0 + n * a.cs1] = __float2half_rn(sum);
+      *reinterpret_cast<uint4*>(xs + m * a.xstride + c * 8) = v;
+    }
+    named_bar_sync(kI4ConsumerBar, kI4Consumers * 32);
   }
-  if (tid == 0) atomicExch(&a.counters[cb], 0u);
+  bool xv[NT];  // token nt*8 + g exists
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) xv[nt] = nt * 8 + g < a.M;
+
+  // scale of (row, k) for this lane; fetched one round ahead
+  auto scale_of = [&](int item, int r, int h) -> uint16_t {
+    const int n = item * kI4Rows + g + 8 * h;
+    const int kk = r * kI4RoundK + warp * kI4KIter + 32 * t;
+    if (n >= a.N || kk >= a.K) return 0;
+    const int grp = a.gs_shift >= 0 ? kk >> a.gs_shift : kk / a.gs;
+    return reinterpret_cast<const uint16_t*>(a.s)[n * a.ss0 + grp * a.ss1];
+  };
+  uint16_t sa_n = 0, sb_n = 0;
+  if (total > 0 && !a.tma_scales) {
+    sa_n = scale_of(blockIdx.x, 0, 0);
+    sb_n = scale_of(blockIdx.x, 0, 1);
+  }
+
+  float acc[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+
+  bool dead = false;
+  const int box = warp >> 1;                 // which 128-byte box of the stage
+  const int chunk = ((warp & 1) << 2) + t;   // 16-byte chunk inside the box row
+  const int swz = (chunk ^ g) << 4;          // 128B swizzle: chunk ^ (row % 8), row = g or g+8
+  int q = 0;
+  for (int j = 0; j < my_items; ++j) {
+    const int item = blockIdx.x + j * gridDim.x;
+    for (int r = 0; r < a.rounds; ++r, ++q) {
+      uint32_t s2a = splat16(sa_n), s2b = splat16(sb_n);
+      if (!a.tma_scales) {  // prefetch the next round's scales
+        const int r1 = r + 1 < a.rounds ? r + 1 : 0;
+        const int it1 = r + 1 < a.rounds ? item : item + gridDim.x;
+        const bool more = q + 1 < total;
+        sa_n = more ? scale_of(it1, r1, 0) : 0;
+        sb_n = more ? scale_of(it1, r1, 1) : 0;
+      }
+      const int st = q % kI4Stages;
+      if (!dead) dead = !__all_sync(0xffffffffu, mbar_wait(&bars->full[st], (q / kI4Stages) & 1, a.err));
+      const uint8_t* sbase = stages + st * kI4StageBytes + box * (kI4Rows * kI4BoxBytes);
+      const uint4 qa4 = *reinterpret_cast<const uint4*>(sbase + g * kI4BoxBytes + swz);
+      const uint4 qb4 = *reinterpret_cast<const uint4*>(sbase + (g + 8) * kI4BoxBytes + swz);
+      if (a.tma_scales) {  // [16 rows][8 groups]: this warp's group is `warp`
+        const uint16_t* sc = reinterpret_cast<const uint16_t*>(sstages + st * kI4ScaleBytes);
+        s2a = splat16(sc[g * 8 + warp]);
+        s2b = splat16(sc[(g + 8) * 8 + warp]);
+      }
+      // The stage is released before these values are used, and the next write to it
+      // is a TMA (async proxy) write: order this thread's generic reads before it.
+      fence_proxy_async_smem();
+      mbar_arrive(&bars->empty[st]);
+      const int kk = r * kI4RoundK + warp * kI4KIter + 32 * t;  // this lane's x column
+      const bool kval = kk < a.K;
+      const uint32_t wa4[4] = {qa4.x, qa4.y, qa4.z, qa4.w};
+      const uint32_t wb4[4] = {qb4.x, qb4.y, qb4.z, qb4.w};
+#pragma unroll
+      for (int wd = 0; wd < 4; ++wd) {
+        uint32_t ba[4], bb[4];
+        if constexpr (kSmemX) {
+          dequant_word_perm(wa4[wd], s2a, ba);
+          dequant_word_perm(wb4[wd], s2b, bb);
+        } else {
+          dequant_word(wa4[wd], s2a, ba);
+          dequant_word(wb4[wd], s2b, bb);
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          // B = x^T: token nt*8 + g, this lane's 8 k (pair order matching ba/bb)
+          uint4 u = make_uint4(0u, 0u, 0u, 0u);
+          const int tok = nt * 8 + g;
+          if constexpr (kSmemX) {
+            if (xv[nt]) u = *reinterpret_cast<const uint4*>(xs + tok * a.xstride + kk + 8 * wd);
+          } else {
+            if (xv[nt] && kval)
+              u = __ldg(reinterpret_cast<const uint4*>(a.x + tok * a.xs0 + kk + 8 * wd));
+          }
+          // A = weights: rows g (ba) and g+8 (bb), two k pairs each
+          mma_16816(acc[nt], ba[0], bb[0], ba[1], bb[1], u.x, u.y);
+          mma_16816(acc[nt], ba[2], bb[2], ba[3], bb[3], u.z, u.w);
+        }
+      }
+    }
+    // ---- item done: add the 8 warps' partial sums in warp order, store fp16
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        // C^T fragment: weight row g + 8*(e>>1), token nt*8 + 2t + (e&1)
+        red[warp][nt * 8 + 2 * t + (e & 1)][g + (e >> 1) * 8] = acc[nt][e];
+        acc[nt][e] = 0.f;
+      }
+    named_bar_sync(kI4ConsumerBar, kI4Consumers * 32);
+    const int nbase = item * kI4Rows;
+    for (int i = tid; i < a.M * kI4Rows; i += kI4Consumers * 32) {
+      const int m = i / kI4Rows, rr = i - m * kI4Rows, n = nbase + rr;
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < kI4Consumers; ++w) sum += red[w][m][rr];
+      if (n < a.N) a.c[m * a.cs0 + n * a.cs1] = __float2half_rn(sum);
+    }
+    named_bar_sync(kI4ConsumerBar, kI4Consumers * 32);
+  }
 }
 
 // Storage dequantizer: one thread per packed word (8 consecutive k of one row).
@@ -232,75 +339,69 @@ __global__ void __launch_bounds__(256) int4_dequant_kernel(const uint8_t* w, con
     const int k = (int)(i - n * words_per_row) * 8;
     const uint32_t q = *reinterpret_cast<const uint32_t*>(w + n * ws0 + k / 2);
     uint32_t p[4];
-    dequant_word(q, __half2half2(s[n * ss0 + (k / gs) * ss1]), p);
-    uint4 o;  // back to natural order: (k0,k1) (k2,k3) (k4,k5) (k6,k7)
-    o.x = __byte_perm(p[0], p[1], 0x5410);
-    o.y = __byte_perm(p[2], p[3], 0x5410);
-    o.z = __byte_perm(p[0], p[1], 0x7632);
-    o.w = __byte_perm(p[2], p[3], 0x7632);
-    *reinterpret_cast<uint4*>(out + n * os0 + k) = o;
+    dequant_word(q, splat16(__half_as_ushort(s[n * ss0 + (k / gs) * ss1])), p);
+    *reinterpret_cast<uint4*>(out + n * os0 + k) = make_uint4(p[0], p[1], p[2], p[3]);
   }
 }
 
-struct I4Plan {
-  int cbs, splits, ks, mt, npad;
-  size_t counter_bytes, partial_bytes;
-};
+constexpr size_t kI4SmemOptin = 232448;  // per-block shared memory limit (227 KB)
+constexpr size_t kI4SmemFixed =
+    1024 + (size_t)kI4Stages * (kI4StageBytes + kI4ScaleBytes) + 256;
 
-static I4Plan plan_int4(int64_t m, int64_t n, int64_t k) {
-  I4Plan p;
-  p.cbs = (int)((n + kI4Cols - 1) / kI4Cols);
-  p.npad = p.cbs * kI4Cols;
-  p.mt = (int)((m + 15) / 16);
-  const int iters_total = (int)((k + kI4KIter - 1) / kI4KIter);
-  const int target = 2 * sm_count();
-  int splits = (target + p.cbs - 1) / p.cbs;
-  if (splits < 1) splits = 1;
-  if (splits > iters_total) splits = iters_total;
-  int iters = (iters_total + splits - 1) / splits;
-  if (iters > kI4MaxIters) iters = kI4MaxIters;
-  splits = (iters_total + iters - 1) / iters;
-  p.splits = splits;
-  p.ks = iters * kI4KIter;
-  // The counters sit in a fixed region that only ever holds counters, whatever the
-  // shape: a region sized per call would overlap the previous call's partial sums.
-  p.counter_bytes = splits > 1 ? (size_t)kI4MaxCounters * 4 : 0;
-  p.partial_bytes = splits > 1 ? (size_t)splits * (size_t)m * (size_t)p.npad * 4 : 0;
-  return p;
+// Largest staged x for an instance: the limit minus the ring, the barriers and the
+// static reduction buffer (8 warps x 8*NT tokens x 17 floats), less 1 KB of margin.
+template <int NT>
+constexpr size_t i4_smem_x_max() {
+  return kI4SmemOptin - kI4SmemFixed - (size_t)kI4Consumers * NT * 8 * (kI4Rows + 1) * 4 - 1024;
 }
 
-// Opts the MT instance in to its largest staging buffer (once per device), launches.
-template <int MT>
-static int launch_int4_gemm(dim3 grid, size_t smem, cudaStream_t st, const I4Args& a) {
+static size_t i4_smem_bytes(bool smem_x, const I4Args& a) {
+  return kI4SmemFixed + (smem_x ? (size_t)a.M * (size_t)a.xstride * 2 : 0);
+}
+
+// Opts each instance in to its largest shared-memory layout (once per device), sizes
+// the persistent grid with the occupancy calculator for this call's layout, launches.
+template <int NT, bool kSmemX>
+static int launch_int4_gemm(cudaStream_t st, const CUtensorMap& tm, const CUtensorMap& tms,
+                            const I4Args& a) {
   static bool attr_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    const int max_smem = MT * 16 * (kI4MaxIters * kI4KIter / 8 + 1) * 16;
-    cudaError_t e = cudaFuncSetAttribute(int4_gemm_kernel<MT>,
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!attr_done[dev]) {
+    const int max_smem = (int)(kI4SmemFixed + (kSmemX ? i4_smem_x_max<NT>() : 0));
+    cudaError_t e = cudaFuncSetAttribute(int4_gemm_kernel<NT, kSmemX>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
     if (e != cudaSuccess) return cuda_fail(e, "fi_int4_gemm: cudaFuncSetAttribute");
     attr_done[dev] = true;
   }
-  int4_gemm_kernel<MT><<<grid, kI4Threads, smem, st>>>(a);
+  const size_t smem = i4_smem_bytes(kSmemX, a);
+  int nb = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, int4_gemm_kernel<NT, kSmemX>,
+                                                    kI4Threads, smem) != cudaSuccess || nb < 1)
+    nb = 1;
+  const int items = (a.N + kI4Rows - 1) / kI4Rows;
+  int grid = nb * sm_count();
+  if (grid > items) grid = items;
+  int4_gemm_kernel<NT, kSmemX><<<(unsigned)grid, kI4Threads, smem, st>>>(tm, tms, a);
   return FI_OK;
 }
 
-}  // namespace fi
-
-extern "C" size_t fi_int4_gemm_workspace_size(int64_t m, int64_t n, int64_t k,
-                                              int64_t groupsize) {
-  (void)groupsize;
-  if (m <= 0 || n <= 0 || k <= 0 || m > fi::kI4MaxM) return 0;
-  const fi::I4Plan p = fi::plan_int4(m, n, k);
-  return p.counter_bytes + p.partial_bytes;
+template <int NT>
+static int launch_int4_gemm_nt(cudaStream_t st, const CUtensorMap& tm, const CUtensorMap& tms,
+                               const I4Args& a) {
+  if ((size_t)a.M * (size_t)a.xstride * 2 <= i4_smem_x_max<NT>())
+    return launch_int4_gemm<NT, true>(st, tm, tms, a);
+  return launch_int4_gemm<NT, false>(st, tm, tms, a);
 }
+
+}  // namespace fi
 
 extern "C" int fi_int4_gemm(const void* x, const void* packed, const void* scales, void* c,
                             int64_t m, int64_t n, int64_t k, int64_t groupsize,
                             const int64_t* x_strides, const int64_t* packed_strides,
                             const int64_t* scales_strides, const int64_t* c_strides,
-                            void* workspace, size_t workspace_bytes, void* stream) {
+                            int32_t* error_flag, void* stream) {
   using namespace fi;
   clear_error();
   if (m < 0 || n < 0 || k <= 0 || groupsize <= 0)
@@ -314,9 +415,8 @@ extern "C" int fi_int4_gemm(const void* x, const void* packed, const void* scale
     return fail(FI_ERR_UNSUPPORTED, "fi_int4_gemm: M (%lld) > %d; dequantize and use a dense GEMM",
                 (long long)m, kI4MaxM);
   if (m == 0 || n == 0) return FI_OK;
-  if (n > (int64_t)kI4MaxCounters * kI4Cols || k > (1 << 30))
-    return fail(FI_ERR_UNSUPPORTED, "fi_int4_gemm: N above %d or K above 2^30",
-                kI4MaxCounters * kI4Cols);
+  if (n > (1 << 30) || k > (1 << 30))
+    return fail(FI_ERR_UNSUPPORTED, "fi_int4_gemm: sizes too large");
   if (!x || !packed || !scales || !c || !x_strides || !packed_strides || !scales_strides ||
       !c_strides)
     return fail(FI_ERR_INVALID_ARG, "fi_int4_gemm: null pointer argument");
@@ -328,46 +428,66 @@ extern "C" int fi_int4_gemm(const void* x, const void* packed, const void* scale
     return fail(FI_ERR_ALIGNMENT,
                 "fi_int4_gemm packed: needs a 16-byte aligned base, unit stride along K/2 and a "
                 "row stride that is a multiple of 16 bytes");
-  const I4Plan p = plan_int4(m, n, k);
-  if (p.splits > 1) {
-    if (!workspace || workspace_bytes < p.counter_bytes + p.partial_bytes)
-      return fail(FI_ERR_WORKSPACE, "fi_int4_gemm: workspace needs %zu bytes, got %zu",
-                  p.counter_bytes + p.partial_bytes, workspace_bytes);
-    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
-      return fail(FI_ERR_ALIGNMENT, "fi_int4_gemm: workspace must be 256-byte aligned");
+  // packed [N, K/2] bytes through a tensor map with 128B swizzle. When K/2 is a whole
+  // number of 128-byte chunks: 3-D (byte, row, chunk), one 4-chunk x 16-row box per
+  // stage; otherwise 2-D (byte, row) with four 128 x 16 boxes (the 3-D view would let
+  // the last chunk of the last row run past the tensor).
+  CUtensorMap tm;
+  const int tma3d = (k / 2) % kI4BoxBytes == 0 ? 1 : 0;
+  int r;
+  if (tma3d) {
+    const uint64_t dims[3] = {(uint64_t)kI4BoxBytes, (uint64_t)n,
+                              (uint64_t)(k / 2 / kI4BoxBytes)};
+    const uint64_t sb[2] = {(uint64_t)packed_strides[0], (uint64_t)kI4BoxBytes};
+    const uint32_t box[3] = {(uint32_t)kI4BoxBytes, (uint32_t)kI4Rows, (uint32_t)kI4Boxes};
+    r = encode_tiled(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, packed, dims, sb, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B, "fi_int4_gemm packed");
+  } else {
+    const uint64_t dims[2] = {(uint64_t)(k / 2), (uint64_t)n};
+    const uint64_t sb[1] = {(uint64_t)packed_strides[0]};
+    const uint32_t box[2] = {(uint32_t)kI4BoxBytes, (uint32_t)kI4Rows};
+    r = encode_tiled(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, packed, dims, sb, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B, "fi_int4_gemm packed");
   }
+  if (r != FI_OK) return r;
   I4Args a;
   a.x = static_cast<const __half*>(x);
-  a.w = static_cast<const uint8_t*>(packed);
   a.s = static_cast<const __half*>(scales);
   a.c = static_cast<__half*>(c);
-  a.counters = static_cast<unsigned*>(workspace);
-  a.partial = p.splits > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
-                                                      p.counter_bytes)
-                           : nullptr;
+  a.err = error_flag;
   a.M = (int)m;
   a.N = (int)n;
   a.K = (int)k;
   a.gs = (int)groupsize;
-  a.ks = p.ks;
-  a.splits = p.splits;
-  a.npad = p.npad;
+  a.gs_shift = (groupsize & (groupsize - 1)) == 0 ? __builtin_ctzll((unsigned long long)groupsize) : -1;
+  a.rounds = (int)((k + kI4RoundK - 1) / kI4RoundK);
+  a.xstride = a.rounds * kI4RoundK + 8;
+  a.tma3d = tma3d;
+  // Scales by TMA when one round's 8 groups are whole 16-byte rows of a dense,
+  // 16-byte aligned [N, K/128] tensor (groupsize 128, K a multiple of 1024).
+  CUtensorMap tms;
+  memset(&tms, 0, sizeof(tms));
+  a.tma_scales = groupsize == 128 && k % kI4RoundK == 0 && scales_strides[1] == 1 &&
+                 (scales_strides[0] * 2) % 16 == 0 && aligned16(scales);
+  if (a.tma_scales) {
+    const uint64_t sdims[2] = {(uint64_t)(k / 128), (uint64_t)n};
+    const uint64_t ssb[1] = {(uint64_t)scales_strides[0] * 2};
+    const uint32_t sbox[2] = {(uint32_t)(kI4RoundK / 128), (uint32_t)kI4Rows};
+    r = encode_tiled(&tms, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, scales, sdims, ssb, sbox,
+                     CU_TENSOR_MAP_SWIZZLE_NONE, "fi_int4_gemm scales");
+    if (r != FI_OK) return r;
+  }
   a.xs0 = x_strides[0];
-  a.ws0 = packed_strides[0];
   a.ss0 = scales_strides[0];
   a.ss1 = scales_strides[1];
   a.cs0 = c_strides[0];
   a.cs1 = c_strides[1];
-  const size_t smem = (size_t)p.mt * 16 * (p.ks / 8 + 1) * 16;
-  const dim3 grid((unsigned)p.cbs, (unsigned)p.splits);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  int r = FI_OK;
-  switch (p.mt) {
-    case 1: r = launch_int4_gemm<1>(grid, smem, st, a); break;
-    case 2: r = launch_int4_gemm<2>(grid, smem, st, a); break;
-    case 3: r = launch_int4_gemm<3>(grid, smem, st, a); break;
-    default: r = launch_int4_gemm<4>(grid, smem, st, a); break;
-  }
+  // 8-token tiles: 1, 2, 4 or 8
+  if (m <= 8) r = launch_int4_gemm_nt<1>(st, tm, tms, a);
+  else if (m <= 16) r = launch_int4_gemm_nt<2>(st, tm, tms, a);
+  else if (m <= 32) r = launch_int4_gemm_nt<4>(st, tm, tms, a);
+  else r = launch_int4_gemm_nt<8>(st, tm, tms, a);
   if (r != FI_OK) return r;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "fi_int4_gemm launch");

@@ -22,22 +22,9 @@ from __future__ import annotations
 import torch
 
 from fast_infer_b200 import _lib
-from fast_infer_b200._runtime import stream_of, with_device
+from fast_infer_b200._runtime import device_errors, error_word, stream_of, with_device
 
 FUSED_MAX_M = 64
-
-# Split-K workspaces of fi_int4_gemm, one per (device, stream): zero-filled once,
-# left zeroed by every call, grown on demand.
-_workspaces: dict = {}
-
-
-def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
-    key = (device.index, stream)
-    ws = _workspaces.get(key)
-    if ws is None or ws.numel() < nbytes:
-        ws = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
-        _workspaces[key] = ws
-    return ws
 
 
 def _check_int4(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, groupsize: int):
@@ -83,16 +70,15 @@ def _fused_int4_matmul(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tens
     if M == 0 or N == 0:
         return c.reshape(*orig_shape[:-1], N)
     lib = _lib.load()
-    need = int(lib.fi_int4_gemm_workspace_size(M, N, K, groupsize))
     with with_device(x.device):
-        stream = stream_of(x.device)
-        ws = _workspace(x.device, stream, need) if need > 0 else None
+        err = error_word(x.device)
         st = lib.fi_int4_gemm(
             x2.data_ptr(), packed.data_ptr(), scales.data_ptr(), c.data_ptr(), M, N, K,
             int(groupsize), _lib.strides(*x2.stride()), _lib.strides(*packed.stride()),
             _lib.strides(*scales.stride()), _lib.strides(*c.stride()),
-            ws.data_ptr() if ws is not None else None, need, stream)
+            err.data_ptr() if err is not None else None, stream_of(x.device))
         _lib.check(st, "int4_matmul")
+        device_errors(err, "int4_matmul")
     return c.reshape(*orig_shape[:-1], N)
 
 

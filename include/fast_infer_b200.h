@@ -216,13 +216,11 @@ int fi_rope_kv_write(const void* qkv, int64_t batch, int64_t seq, int64_t num_q_
  * scales fp16 [N, K/groupsize]; weight value fp16(q * scale). K % groupsize == 0.
  */
 
-/* Bytes of split-K workspace fi_int4_gemm needs for these sizes (0 = none). */
-size_t fi_int4_gemm_workspace_size(int64_t m, int64_t n, int64_t k, int64_t groupsize);
-
 /*
  * C[M, N] = x[M, K] @ dequant(W)^T, fp16 in / fp16 out, fp32 accumulation, for
  * decode-sized M (1..64; larger M returns FI_ERR_UNSUPPORTED — dequantize with
- * fi_int4_dequant and use a dense GEMM).
+ * fi_int4_dequant and use a dense GEMM). Uses no workspace; deterministic.
+ * error_flag: optional device int32; FI_DEVERR_TIMEOUT if a pipeline wait ran out.
  *
  * Replaces: kernels/matmul.py:14-132 `_fused_int4_matmul` (reached through
  * `int4_matmul(x, (packed, scales), groupsize)`, kernels/matmul.py:217-231, from
@@ -234,18 +232,11 @@ size_t fi_int4_gemm_workspace_size(int64_t m, int64_t n, int64_t k, int64_t grou
  *           row stride.
  * scales  : [N, K/groupsize] fp16, any strides. groupsize a multiple of 32.
  * c       : [M, N] fp16, any strides.
- * workspace: caller-owned device buffer of fi_int4_gemm_workspace_size(...) bytes,
- *           256-byte aligned. Its first 256 KB hold split-K counters that must be
- *           ZERO before the first use; every call leaves them zero again, so one
- *           workspace serves calls of any shape. Calls sharing a workspace must be
- *           ordered on one stream. N is limited to 65536 * 128.
- * Deterministic: split-K partial sums are added in a fixed order.
  */
 int fi_int4_gemm(const void* x, const void* packed, const void* scales, void* c, int64_t m,
                  int64_t n, int64_t k, int64_t groupsize, const int64_t* x_strides,
                  const int64_t* packed_strides, const int64_t* scales_strides,
-                 const int64_t* c_strides, void* workspace, size_t workspace_bytes,
-                 void* stream);
+                 const int64_t* c_strides, int32_t* error_flag, void* stream);
 
 /*
  * Dequantize INT4 weights to fp16 [N, K] (out_strides {row, 1}; 16-byte aligned base,

@@ -105,35 +105,27 @@ def test_python_wrappers_reject_cpu_tensors():
     assert out.shape == (1, 2, 128) and not out.any()
 
 
-def test_int4_validation_and_workspace_size():
+def test_int4_validation():
     lib = _lib.load()
     s2 = _lib.strides(16, 1)
     # K not a multiple of groupsize; groupsize not a multiple of 32; M beyond the fused path
-    assert lib.fi_int4_gemm(1, 1, 1, 1, 4, 64, 200, 128, s2, s2, s2, s2, None, 0,
-                            None) == _lib.FI_ERR_INVALID_ARG
-    assert lib.fi_int4_gemm(1, 1, 1, 1, 4, 64, 160, 16, s2, s2, s2, s2, None, 0,
-                            None) == _lib.FI_ERR_UNSUPPORTED
-    assert lib.fi_int4_gemm(1, 1, 1, 1, 65, 64, 256, 128, s2, s2, s2, s2, None, 0,
-                            None) == _lib.FI_ERR_UNSUPPORTED
+    assert lib.fi_int4_gemm(1, 1, 1, 1, 4, 64, 200, 128, s2, s2, s2, s2,
+                            None, None) == _lib.FI_ERR_INVALID_ARG
+    assert lib.fi_int4_gemm(1, 1, 1, 1, 4, 64, 160, 16, s2, s2, s2, s2,
+                            None, None) == _lib.FI_ERR_UNSUPPORTED
+    assert lib.fi_int4_gemm(1, 1, 1, 1, 65, 64, 256, 128, s2, s2, s2, s2,
+                            None, None) == _lib.FI_ERR_UNSUPPORTED
     assert b"dense GEMM" in lib.fi_last_error()
     # misaligned x row stride / packed row stride, null pointers
     assert lib.fi_int4_gemm(16, 16, 16, 16, 4, 64, 256, 128, _lib.strides(260, 1), s2, s2, s2,
-                            None, 0, None) == _lib.FI_ERR_ALIGNMENT
+                            None, None) == _lib.FI_ERR_ALIGNMENT
     assert lib.fi_int4_gemm(16, 16, 16, 16, 4, 64, 256, 128, _lib.strides(256, 1),
-                            _lib.strides(130, 1), s2, s2, None, 0, None) == _lib.FI_ERR_ALIGNMENT
-    assert lib.fi_int4_gemm(None, 16, 16, 16, 4, 64, 256, 128, s2, s2, s2, s2, None, 0,
-                            None) == _lib.FI_ERR_INVALID_ARG
+                            _lib.strides(130, 1), s2, s2, None, None) == _lib.FI_ERR_ALIGNMENT
+    assert lib.fi_int4_gemm(None, 16, 16, 16, 4, 64, 256, 128, s2, s2, s2, s2,
+                            None, None) == _lib.FI_ERR_INVALID_ARG
     # empty problems are a no-op
-    assert lib.fi_int4_gemm(None, None, None, None, 0, 64, 256, 128, s2, s2, s2, s2, None, 0,
-                            None) == _lib.FI_OK
-    # split-K workspace: counters + [splits, M, Npad] fp32; none beyond the fused path
-    need = lib.fi_int4_gemm_workspace_size(16, 3072, 3072, 128)
-    assert need > 0 and need % 4 == 0
-    assert lib.fi_int4_gemm_workspace_size(65, 3072, 3072, 128) == 0
-    # a too-small workspace is refused before any device work
-    assert lib.fi_int4_gemm(16, 16, 16, 16, 16, 3072, 3072, 128, _lib.strides(3072, 1),
-                            _lib.strides(1536, 1), _lib.strides(24, 1), _lib.strides(3072, 1),
-                            None, 0, None) == _lib.FI_ERR_WORKSPACE
+    assert lib.fi_int4_gemm(None, None, None, None, 0, 64, 256, 128, s2, s2, s2, s2,
+                            None, None) == _lib.FI_OK
     # dequant / quantize argument checks
     assert lib.fi_int4_dequant(1, 1, 1, 8, 200, 128, s2, s2, s2, None) == _lib.FI_ERR_INVALID_ARG
     assert lib.fi_int4_dequant(1, 1, 16, 8, 256, 128, _lib.strides(128, 1), s2,

@@ -137,20 +137,15 @@ def test_strided_operands_and_batched_input(cuda_device):
     lib = _lib.load()
     xd, pd, sd = _dev(x, cuda_device), _dev(packed, cuda_device), _dev(scales, cuda_device)
     ct = torch.empty(n, m, dtype=torch.float16, device=cuda_device).t()
-    need = lib.fi_int4_gemm_workspace_size(m, n, k, 128)
-    ws = torch.zeros(max(need, 1), dtype=torch.uint8, device=cuda_device)
     st = lib.fi_int4_gemm(xd.data_ptr(), pd.data_ptr(), sd.data_ptr(), ct.data_ptr(), m, n, k,
                           128, _lib.strides(*xd.stride()), _lib.strides(*pd.stride()),
-                          _lib.strides(*sd.stride()), _lib.strides(*ct.stride()),
-                          ws.data_ptr(), need, torch.cuda.current_stream().cuda_stream)
+                          _lib.strides(*sd.stride()), _lib.strides(*ct.stride()), None,
+                          torch.cuda.current_stream().cuda_stream)
     assert st == _lib.FI_OK
     assert int4_close(ct.cpu().numpy(), ref)[0]
-    # the workspace's counters are back to zero after the call
-    torch.cuda.synchronize()
-    assert int(ws[:1 << 18].to(torch.int32).abs().sum()) == 0
 
 
-def test_deterministic_and_workspace_reuse(cuda_device):
+def test_deterministic_across_calls_and_shapes(cuda_device):
     from fast_infer_b200.kernels.matmul import int4_matmul as gpu_mm
     shapes = [(3072, 8192, 16), (5120, 3072, 1), (3072, 8192, 16), (16384, 3072, 64)]
     first = {}
