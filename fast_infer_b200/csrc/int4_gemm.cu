@@ -350,9 +350,14 @@ constexpr size_t kI4SmemFixed =
 
 // Largest staged x for an instance: the limit minus the ring, the barriers and the
 // static reduction buffer (8 warps x 8*NT tokens x 17 floats), less 1 KB of margin.
+#ifndef FI_I4_XMAX_KB
+#define FI_I4_XMAX_KB 1024
+#endif
 template <int NT>
 constexpr size_t i4_smem_x_max() {
-  return kI4SmemOptin - kI4SmemFixed - (size_t)kI4Consumers * NT * 8 * (kI4Rows + 1) * 4 - 1024;
+  constexpr size_t fit =
+      kI4SmemOptin - kI4SmemFixed - (size_t)kI4Consumers * NT * 8 * (kI4Rows + 1) * 4 - 1024;
+  return fit < (size_t)FI_I4_XMAX_KB * 1024 ? fit : (size_t)FI_I4_XMAX_KB * 1024;
 }
 
 static size_t i4_smem_bytes(bool smem_x, const I4Args& a) {
