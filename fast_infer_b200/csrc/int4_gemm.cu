@@ -141,8 +141,10 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, uin
 // fragments come from global memory in natural order and dequant_word is used.
 // Every mbarrier wait is bounded: after a timeout (FI_DEVERR_TIMEOUT) the waits are
 // skipped, the loops still run to the end and the producer lets its copies land.
+// Up to 8 tokens the kernel fits 56 registers, so up to 4 CTAs share an SM (the ring
+// and staged x then decide); larger token tiles run one CTA per SM.
 template <int NT, bool kSmemX>
-__global__ void __launch_bounds__(kI4Threads, 1)
+__global__ void __launch_bounds__(kI4Threads, NT == 1 ? 4 : 1)
     int4_gemm_kernel(const __grid_constant__ CUtensorMap tm_w,
                      const __grid_constant__ CUtensorMap tm_s, const I4Args a) {
   extern __shared__ uint8_t smem_raw[];
