@@ -60,6 +60,7 @@ SIGNATURES = {
     "fi_kv_write": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64,
                                    _i64, _i64, _i64, _i64, _i64p, _i64p, _i64p, _i64p, _i64p,
                                    _vp, _vp]),
+    "fi_rms_norm": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _vp]),
     "fi_int4_gemm": (ctypes.c_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64p, _i64p,
                                     _i64p, _i64p, _vp, _vp]),
     "fi_int4_dequant": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64p, _i64p, _i64p,

@@ -18,11 +18,12 @@ input of token t+1 (there is no embedding or sampler in an attention-only stack)
 Weights are random N(0, 0.02) fp16 drawn on the device from a fixed seed, identical
 on every rank (same GPU model), then sliced to the rank's heads.
 
-The projections and RMSNorm use PyTorch (cuBLAS GEMMs; RMSNorm follows reference
-kernels/rms_norm.py:8-43, fp32 math, fp16 out); they are outside the path this
-library implements. RoPE (reference kernels/rope.py:9-44) and the KV slot write are
-one fused kernel (``rope_and_store`` / fi_rope_kv_write), bit-identical to the
-reference's fp16 ops. ``apply_rope`` below restates the reference's RoPE for tests.
+The projections are cuBLAS GEMMs through PyTorch (the residual add rides in the O
+projection's GEMM as beta = 1); RMSNorm is one launch of ``fi_rms_norm`` (reference
+kernels/rms_norm.py:8-43, fp32 math, fp16 out). RoPE (reference kernels/rope.py:9-44)
+and the KV slot write are one fused kernel (``rope_and_store`` / fi_rope_kv_write),
+bit-identical to the reference's fp16 ops. ``apply_rope`` and ``rms_norm_torch``
+below restate the reference's RoPE and RMSNorm in PyTorch for tests.
 """
 
 from __future__ import annotations
@@ -33,6 +34,7 @@ import torch
 
 from fast_infer_b200._runtime import device_checks
 from fast_infer_b200.kernels.attention import flash_attention, paged_attention
+from fast_infer_b200.kernels.rms_norm import rms_norm
 from fast_infer_b200.kv_cache import KVCache, rope_and_store
 from fast_infer_b200.shard import HeadShard, gather_heads, head_shard
 
@@ -54,7 +56,7 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
     return x * cos.unsqueeze(1) + rot * sin.unsqueeze(1)
 
 
-def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+def rms_norm_torch(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     """x * rsqrt(mean(x^2) + eps) * w in fp32, fp16 out (reference kernels/rms_norm.py)."""
     xf = x.float()
     return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(x.dtype)
@@ -108,6 +110,11 @@ class AttentionStack:
     def _gather(self, o: torch.Tensor) -> torch.Tensor:
         return o if self.world == 1 else self.gather(o)
 
+    @staticmethod
+    def _residual(h: torch.Tensor, o: torch.Tensor, wo: torch.Tensor) -> None:
+        """h += o @ wo as one GEMM with beta = 1 (h contiguous, updated in place)."""
+        h.view(-1, h.shape[-1]).addmm_(o.reshape(-1, o.shape[-1]), wo)
+
     # ------------------------------------------------------------------ prefill
     def _qkv(self, w, h):
         return rms_norm(h, w["norm"], self.eps) @ w["wqkv"]
@@ -124,13 +131,14 @@ class AttentionStack:
             self.cache._ensure_blocks(b, need)
         self.cache.num_tokens = S
         k_rot = torch.empty(B, S, nkv, D, dtype=torch.float16, device=self.device)
+        h = h.contiguous().clone()  # the residual stream is updated in place below
         for li, w in enumerate(self.layers):
             qkv = self._qkv(w, h)
             q_rot = rope_and_store(self.cache, li, qkv, nq, self.cos, self.sin, 0, k_out=k_rot)
             v = qkv[..., (nq + nkv) * D:].view(B, S, nkv, D)
             o = flash_attention(q_rot.transpose(1, 2), k_rot.transpose(1, 2), v.transpose(1, 2))
             o = self._gather(o.transpose(1, 2).reshape(B, S, nq * D))
-            h = h + o @ w["wo"]
+            self._residual(h, o, w["wo"])
         self.token_count = S
         return h
 
@@ -157,7 +165,7 @@ class AttentionStack:
         B = self.batch
         nq, D = self.shard.num_q_heads, self.D
         span = self.cache.max_blocks_per_seq * 64
-        h = self._h_in
+        h = self._h_in.clone()  # the residual stream is updated in place below
         for li, w in enumerate(self.layers):
             q = rope_and_store(self.cache, li, self._qkv(w, h), nq, self.cos, self.sin,
                                self._dev_start)
@@ -165,7 +173,7 @@ class AttentionStack:
                                 self.cache.block_table, 64, 0, context_lens=self._dev_ctx,
                                 max_context_len=span, workspace=self._ws)
             o = self._gather(o.reshape(B, 1, nq * D))
-            h = h + o @ w["wo"]
+            self._residual(h, o, w["wo"])
         self._dev_ctx.add_(1)
         self._dev_start.add_(1)
         self._h_in.copy_(h)

@@ -207,6 +207,17 @@ int fi_rope_kv_write(const void* qkv, int64_t batch, int64_t seq, int64_t num_q_
                      const int64_t* vc_strides, const int64_t* bt_strides, int32_t* error_flag,
                      void* stream);
 
+/*
+ * RMSNorm: out[r, :] = x[r, :] * rsqrt(mean(x[r, :]^2) + eps) * weight, fp16 in/out,
+ * fp32 arithmetic. x, out: [rows, hidden] with row strides (elements, multiples of 8;
+ * unit inner stride); weight: [hidden]. hidden a multiple of 8; 16-byte aligned bases.
+ *
+ * Replaces: kernels/rms_norm.py:29-43 `rms_norm(x, weight, eps)` (called at
+ * model.py:82,141,153), used here by the attention-stack harness.
+ */
+int fi_rms_norm(const void* x, const void* weight, void* out, int64_t rows, int64_t hidden,
+                int64_t x_row_stride, int64_t out_row_stride, float eps, void* stream);
+
 /* ---- INT4 group-wise weights (the projections around attention) ---------- */
 
 /*

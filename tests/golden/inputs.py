@@ -111,3 +111,16 @@ def int4_inputs(name: str):
         w[1, 3] = np.float16(5.0)
     xs = {m: randn_f16(rng, (m, k)) for m in ms}
     return w, xs, g
+
+
+# RMSNorm fixture: (rows, hidden) shapes; row 0 of the first case carries large values.
+RMS_CASES = ((4, 3072), (7, 128))
+
+
+def rms_inputs(rows: int, hidden: int):
+    rng = np.random.default_rng(71 + rows + hidden)
+    x = randn_f16(rng, (rows, hidden))
+    if hidden == 3072:
+        x[0] = (x[0].astype(np.float32) * 40.0).astype(np.float16)
+    w = (1.0 + 0.1 * rng.standard_normal(size=(hidden,), dtype=np.float32)).astype(np.float16)
+    return x, w

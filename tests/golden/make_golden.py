@@ -21,6 +21,8 @@ Fixtures:
 * ``rope.npz``          the reference's ``apply_rope`` (kernels/rope.py) on a 6-token
                         prefill and a decode token at position 300, with the fp16
                         cos/sin rows model.py:74-75 feeds it.
+* ``rms_norm.npz``      the reference's ``rms_norm`` Triton kernel (kernels/rms_norm.py)
+                        on the ``RMS_CASES`` shapes.
 * ``int4.npz``          the reference's ``quantize_int4_groupwise`` and
                         ``dequantize_int4`` (loader.py), ``_dequant_storage`` and the
                         fused ``int4_matmul`` Triton kernel (kernels/matmul.py) on the
@@ -42,9 +44,9 @@ HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parent.parent))
 
 from tests.golden.inputs import (  # noqa: E402
-    DECODE_RAGGED_LENS, INT4_CASES, KV_WRITE, PREFILL_SMALL_S, ROPE_DECODE_POS, ROPE_PREFILL_POS,
-    c1_inputs, decode_ragged_inputs, int4_inputs, kv_write_inputs, prefill_small_inputs,
-    rope_inputs)
+    DECODE_RAGGED_LENS, INT4_CASES, KV_WRITE, PREFILL_SMALL_S, RMS_CASES, ROPE_DECODE_POS,
+    ROPE_PREFILL_POS, c1_inputs, decode_ragged_inputs, int4_inputs, kv_write_inputs,
+    prefill_small_inputs, rms_inputs, rope_inputs)
 
 
 def _import_reference(ref_path: str):
@@ -73,16 +75,18 @@ def digest(a: np.ndarray) -> str:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
-    ap.add_argument("--only", choices=["attention", "int4"], default=None,
+    ap.add_argument("--only", choices=["attention", "int4", "rms_norm"], default=None,
                     help="regenerate one group of fixtures (default: all)")
     args = ap.parse_args()
     ref_attn, ref_kv, ref_model, ref_rope = _import_reference(args.reference)
     import torch
     T = torch.from_numpy
-    if args.only != "int4":
+    if args.only in (None, "attention"):
         _attention_fixtures(ref_attn, ref_kv, ref_model, ref_rope, torch, T)
-    if args.only != "attention":
+    if args.only in (None, "int4"):
         _int4_fixtures(T)
+    if args.only in (None, "rms_norm"):
+        _rms_fixtures(T)
     print("golden fixtures written to", HERE)
 
 
@@ -177,6 +181,16 @@ def _attention_fixtures(ref_attn, ref_kv, ref_model, ref_rope, torch, T):
                         dcos16=dc16.numpy(), dsin16=ds16.numpy(), q_rot=qr.numpy(),
                         k_rot=kr.numpy(), dq_rot=dqr.numpy(), dk_rot=dkr.numpy(),
                         cos_fp32_row300=cos[ROPE_DECODE_POS].numpy())
+
+
+def _rms_fixtures(T):
+    """The reference's RMSNorm Triton kernel."""
+    from fast_infer.kernels import rms_norm as ref_rms  # type: ignore
+    out = {}
+    for rows, hidden in RMS_CASES:
+        x, w = rms_inputs(rows, hidden)
+        out[f"out_{rows}x{hidden}"] = ref_rms.rms_norm(T(x), T(w), 1e-5).numpy()
+    np.savez_compressed(HERE / "rms_norm.npz", **out)
 
 
 def _int4_fixtures(T):

@@ -13,7 +13,7 @@ pytestmark = pytest.mark.gpu
 def _fp32_attention_stack(stack, prompt, steps):
     """Same weights and torch ops as AttentionStack, attention = dense fp32 softmax
     over every cached token (K/V kept as the fp16 values the stack stores)."""
-    from fast_infer_b200.stack import apply_rope, rms_norm
+    from fast_infer_b200.stack import apply_rope, rms_norm_torch as rms_norm
     B, S, H = prompt.shape
     D, hq, hkv = stack.D, stack.shard.num_q_heads, stack.shard.num_kv_heads
     G = hq // hkv
