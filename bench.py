@@ -485,24 +485,35 @@ def run_stack(torch, dev, rank, world, dist, warmup=1):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    # prefill timed three times (each pass resets the cache), median kept; the decode
+    # steps continue from the last prefill
+    pf = []
+    for _ in range(3):
+        sync_all()
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        e[0].record()
+        h = st.prefill(prompt)[:, -1:]
+        e[1].record()
+        torch.cuda.synchronize()
+        pf.append(max_ms(e[0].elapsed_time(e[1])))
+    pf_ms = sorted(pf)[1]
     sync_all()
-    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     e[0].record()
-    h = st.prefill(prompt)[:, -1:]
-    e[1].record()
     st.begin_decode(h)
     for _ in range(STACK_STEPS):
         h = st.decode_step(use_graph=use_graph)
-    e[2].record()
+    e[1].record()
     torch.cuda.synchronize()
-    pf_ms, dec_ms = max_ms(e[0].elapsed_time(e[1])), max_ms(e[1].elapsed_time(e[2]))
+    dec_ms = max_ms(e[0].elapsed_time(e[1]))
     finite = bool(torch.isfinite(h).all().item())
     st.release_graph()
     sync_all()
     return {
         "workload": "config 4: 28-layer attention stack (Llama-3.2-3B attention shapes, random "
                     "weights), B16, prefill 1024 then 256 decode steps, KV heads sharded over "
-                    f"{world} GPU(s), NCCL all-gather of head outputs per layer",
+                    f"{world} GPU(s), NCCL all-gather of head outputs per layer; prefill = median "
+                    "of 3 timed passes",
         "scaling": "strong",
         "prefill_ms": round(pf_ms, 3),
         "prefill_tokens_per_s": round(STACK_BATCH * STACK_PROMPT / (pf_ms * 1e-3), 1),

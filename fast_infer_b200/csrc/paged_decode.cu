@@ -378,8 +378,13 @@ __global__ void __launch_bounds__(128) paged_decode_combine_kernel(const DecodeP
 // Split size: aim for ~4 waves of 2 CTAs per SM over all (sequence, KV head) pairs.
 static int choose_pps(int64_t batch, int64_t hkv, int64_t max_pages, int64_t requested) {
   if (requested > 0) return (int)(requested < kMaxPagesPerSplit ? requested : kMaxPagesPerSplit);
-  const int64_t target = (int64_t)sm_count() * 2 * 4;
   const int64_t units = batch * hkv > 0 ? batch * hkv : 1;
+  // One CTA per (sequence, KV head) already filling most SMs beats any split: the
+  // combine launch and the partials cost more than the extra parallelism buys
+  // (batch 16 / 32 / 64 x 8 KV heads measured fastest unsplit). Below that, aim at
+  // about two CTAs per SM.
+  if (units * 4 >= (int64_t)sm_count() * 3) return kMaxPagesPerSplit;
+  const int64_t target = (int64_t)sm_count() * 2;
   int64_t splits = (target + units - 1) / units;
   if (splits < 1) splits = 1;
   int64_t pps = (max_pages + splits - 1) / splits;

@@ -4,10 +4,11 @@
 // :8-26) as called at model.py:82,141,153: fp16 in, fp32 arithmetic in the
 // reference's order ((x * rms) * weight), fp16 out.
 //
-// One warp per row: the lanes stride over the row in 16-byte vectors, sum x^2 in
-// fp32, reduce with shuffles, then read the row again (an L1 hit) to scale it. Rows
-// are independent, so any number of rows (decode's batch or prefill's tokens) maps to
-// ceil(rows / 8) CTAs of 8 warps.
+// One warp per row: the lanes take the row in 16-byte vectors, sum x^2 in fp32,
+// reduce with shuffles and scale. Rows of up to 4096 elements are held in registers
+// (every load of a lane issued before the first use, one pass over memory); longer
+// rows loop and read the row twice. Rows are independent, so any number of rows
+// (decode's batch or prefill's tokens) maps to ceil(rows / 8) CTAs of 8 warps.
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -16,6 +17,60 @@
 namespace fi {
 
 constexpr int kRmsWarps = 8;
+
+// Rows of hidden <= VPL * 256 elements: each lane holds VPL 16-byte vectors.
+template <int VPL>
+__global__ void __launch_bounds__(kRmsWarps * 32)
+    rms_norm_reg_kernel(const __half* x, const __half* w, __half* out, int64_t rows, int hidden,
+                        int64_t xs0, int64_t os0, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kRmsWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const __half* xr = x + row * xs0;
+  __half* orow = out + row * os0;
+  const int vecs = hidden / 8;
+  uint4 xv[VPL], wv[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int v = lane + 32 * i;
+    xv[i] = make_uint4(0u, 0u, 0u, 0u);
+    wv[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (v < vecs) {
+      xv[i] = *reinterpret_cast<const uint4*>(xr + v * 8);
+      wv[i] = __ldg(reinterpret_cast<const uint4*>(w + v * 8));
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const __half2* h = reinterpret_cast<const __half2*>(&xv[i]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(h[e]);
+      ss = fmaf(f.x, f.x, ss);
+      ss = fmaf(f.y, f.y, ss);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float rms = rsqrtf(ss / (float)hidden + eps);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int v = lane + 32 * i;
+    if (v >= vecs) break;
+    const __half2* h = reinterpret_cast<const __half2*>(&xv[i]);
+    const __half2* wh = reinterpret_cast<const __half2*>(&wv[i]);
+    uint4 o;
+    __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(h[e]);
+      const float2 g = __half22float2(wh[e]);
+      oh[e] = __floats2half2_rn(f.x * rms * g.x, f.y * rms * g.y);
+    }
+    *reinterpret_cast<uint4*>(orow + v * 8) = o;
+  }
+}
 
 __global__ void __launch_bounds__(kRmsWarps * 32)
     rms_norm_kernel(const __half* x, const __half* w, __half* out, int64_t rows, int hidden,
@@ -76,9 +131,27 @@ extern "C" int fi_rms_norm(const void* x, const void* weight, void* out, int64_t
                 "multiples of 8");
   const int64_t blocks = (rows + kRmsWarps - 1) / kRmsWarps;
   if (blocks > 0x7fffffff) return fail(FI_ERR_UNSUPPORTED, "fi_rms_norm: too many rows");
-  rms_norm_kernel<<<(unsigned)blocks, kRmsWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __half*>(x), static_cast<const __half*>(weight),
-      static_cast<__half*>(out), rows, (int)hidden, x_row_stride, out_row_stride, eps);
+  const __half* xp = static_cast<const __half*>(x);
+  const __half* wp = static_cast<const __half*>(weight);
+  __half* op = static_cast<__half*>(out);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned grid = (unsigned)blocks, block = kRmsWarps * 32;
+  const int vpl = (int)((hidden / 8 + 31) / 32);  // 16-byte vectors per lane
+  if (vpl <= 4)
+    rms_norm_reg_kernel<4><<<grid, block, 0, st>>>(xp, wp, op, rows, (int)hidden, x_row_stride,
+                                                    out_row_stride, eps);
+  else if (vpl <= 8)
+    rms_norm_reg_kernel<8><<<grid, block, 0, st>>>(xp, wp, op, rows, (int)hidden, x_row_stride,
+                                                    out_row_stride, eps);
+  else if (vpl <= 12)
+    rms_norm_reg_kernel<12><<<grid, block, 0, st>>>(xp, wp, op, rows, (int)hidden, x_row_stride,
+                                                     out_row_stride, eps);
+  else if (vpl <= 16)
+    rms_norm_reg_kernel<16><<<grid, block, 0, st>>>(xp, wp, op, rows, (int)hidden, x_row_stride,
+                                                     out_row_stride, eps);
+  else
+    rms_norm_kernel<<<grid, block, 0, st>>>(xp, wp, op, rows, (int)hidden, x_row_stride,
+                                            out_row_stride, eps);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "fi_rms_norm launch");
   return FI_OK;
