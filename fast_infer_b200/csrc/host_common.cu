@@ -1,5 +1,6 @@
 // Host helpers: thread-local error messages, tensor-map encoding, device queries.
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <mutex>
 
@@ -67,6 +68,14 @@ int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, con
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(FI_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, (int)r);
   return FI_OK;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("FI_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
 }
 
 int sm_count() {

@@ -169,12 +169,29 @@ __global__ void __launch_bounds__(kI4Threads, NT == 1 ? 4 : 1)
     fence_barrier_init();
   }
   __syncthreads();
+  // The next projection may start launching now: it only reads weights into L2
+  // until this grid has completed.
+  grid_dep_launch();
 
   if (warp == kI4Consumers) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       prefetch_tmap(&tm_w);
       if (a.tma_scales) prefetch_tmap(&tm_s);
+      // Before the previous kernel on the stream is known to be done (it may have
+      // written these weights), the first ring's worth of weight tiles only goes to
+      // L2; the shared-memory copies start after grid_dep_wait().
+      for (int q = 0; q < total && q < kI4Stages; ++q) {
+        const int item = blockIdx.x + (q / a.rounds) * gridDim.x, r = q % a.rounds;
+        if (a.tma3d) {
+          tma_prefetch_l2_3d(&tm_w, 0, item * kI4Rows, r * kI4Boxes);
+        } else {
+#pragma unroll
+          for (int b = 0; b < kI4Boxes; ++b)
+            tma_prefetch_l2_2d(&tm_w, r * (kI4RoundK / 2) + b * kI4BoxBytes, item * kI4Rows);
+        }
+      }
+      grid_dep_wait();
       bool dead = false;
       for (int q = 0; q < total; ++q) {
         const int st = q % kI4Stages;
@@ -205,6 +222,7 @@ __global__ void __launch_bounds__(kI4Threads, NT == 1 ? 4 : 1)
   }
 
   // ---------------------------------------------------------------- consumers
+  grid_dep_wait();  // x and the scales may be the previous kernel's output
   const int g = lane >> 2, t = lane & 3;
   if constexpr (kSmemX) {
     const int chunks = a.rounds * (kI4RoundK / 8);
@@ -390,7 +408,9 @@ static int launch_int4_gemm(cudaStream_t st, const CUtensorMap& tm, const CUtens
   const int items = (a.N + kI4Rows - 1) / kI4Rows;
   int grid = nb * sm_count();
   if (grid > items) grid = items;
-  int4_gemm_kernel<NT, kSmemX><<<(unsigned)grid, kI4Threads, smem, st>>>(tm, tms, a);
+  cudaError_t e = launch_pdl(int4_gemm_kernel<NT, kSmemX>, dim3((unsigned)grid), dim3(kI4Threads),
+                             smem, st, tm, tms, a);
+  if (e != cudaSuccess) return cuda_fail(e, "fi_int4_gemm launch");
   return FI_OK;
 }
 

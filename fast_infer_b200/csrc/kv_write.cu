@@ -29,6 +29,8 @@ struct KvWriteArgs {
 
 template <bool kVec>
 __global__ void __launch_bounds__(256) kv_write_kernel(const KvWriteArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t chunks_per_row = kVec ? a.head_dim / 8 : a.head_dim;
   const int64_t total = a.batch * a.num_new * a.heads * chunks_per_row;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
@@ -132,11 +134,9 @@ extern "C" int fi_kv_write(const void* k, const void* v, void* k_cache, void* v_
   const int64_t cap = (int64_t)sm_count() * 16;
   if (blocks > cap) blocks = cap;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (vec)
-    kv_write_kernel<true><<<(unsigned)blocks, threads, 0, s>>>(a);
-  else
-    kv_write_kernel<false><<<(unsigned)blocks, threads, 0, s>>>(a);
-  cudaError_t e = cudaGetLastError();
+  const cudaError_t e =
+      vec ? launch_pdl(kv_write_kernel<true>, dim3((unsigned)blocks), dim3(threads), 0, s, a)
+          : launch_pdl(kv_write_kernel<false>, dim3((unsigned)blocks), dim3(threads), 0, s, a);
   if (e != cudaSuccess) return cuda_fail(e, "fi_kv_write launch");
   return FI_OK;
 }

@@ -90,6 +90,8 @@ __global__ void __launch_bounds__(kDecThreads, 2)
 
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  grid_dep_wait();  // lengths, block table, K/V and q may come from the previous kernel
+  grid_dep_launch();
   int ctx;
   const int npages = seq_pages(p, b, ctx, split == 0 && threadIdx.x == 0 && kvh == 0);
   const int pg0 = split * p.pps;
@@ -335,6 +337,8 @@ __global__ void __launch_bounds__(kDecThreads, 2)
 
 // Merge split-KV partials: one warp per (sequence, query head), 4 dims per lane.
 __global__ void __launch_bounds__(128) paged_decode_combine_kernel(const DecodeParams p) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hq = blockIdx.x * 4 + warp, b = blockIdx.y;
   if (hq >= p.hq) return;
@@ -521,13 +525,12 @@ extern "C" int fi_paged_decode(const void* q, const void* k_cache, const void* v
     attr_done[dev] = true;
   }
   dim3 grid((unsigned)max_splits, (unsigned)num_kv_heads, (unsigned)batch);
-  paged_decode_kernel<<<grid, kDecThreads, kDecSmemBytes, s>>>(tmk, tmv, p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(paged_decode_kernel, grid, dim3(kDecThreads), kDecSmemBytes, s, tmk,
+                             tmv, p);
   if (e != cudaSuccess) return cuda_fail(e, "fi_paged_decode: launch");
   if (max_splits > 1) {
     dim3 g2((unsigned)((num_q_heads + 3) / 4), (unsigned)batch);
-    paged_decode_combine_kernel<<<g2, 128, 0, s>>>(p);
-    e = cudaGetLastError();
+    e = launch_pdl(paged_decode_combine_kernel, g2, dim3(128), 0, s, p);
     if (e != cudaSuccess) return cuda_fail(e, "fi_paged_decode: combine launch");
   }
   return FI_OK;

@@ -23,6 +23,8 @@ template <int VPL>
 __global__ void __launch_bounds__(kRmsWarps * 32)
     rms_norm_reg_kernel(const __half* x, const __half* w, __half* out, int64_t rows, int hidden,
                         int64_t xs0, int64_t os0, float eps) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kRmsWarps + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -75,6 +77,8 @@ __global__ void __launch_bounds__(kRmsWarps * 32)
 __global__ void __launch_bounds__(kRmsWarps * 32)
     rms_norm_kernel(const __half* x, const __half* w, __half* out, int64_t rows, int hidden,
                     int64_t xs0, int64_t os0, float eps) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kRmsWarps + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -137,22 +141,22 @@ extern "C" int fi_rms_norm(const void* x, const void* weight, void* out, int64_t
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const unsigned grid = (unsigned)blocks, block = kRmsWarps * 32;
   const int vpl = (int)((hidden / 8 + 31) / 32);  // 16-byte vectors per lane
+  cudaError_t e;
   if (vpl <= 4)
-    rms_norm_reg_kernel<4><<<grid, block, 0, st>>>(xp, wp, op, rows, (int)hidden, x_row_stride,
-                                                    out_row_stride, eps);
+    e = launch_pdl(rms_norm_reg_kernel<4>, grid, block, 0, st, xp, wp, op, rows, (int)hidden,
+                   x_row_stride, out_row_stride, eps);
   else if (vpl <= 8)
-    rms_norm_reg_kernel<8><<<grid, block, 0, st>>>(xp, wp, op, rows, (int)hidden, x_row_stride,
-                                                    out_row_stride, eps);
+    e = launch_pdl(rms_norm_reg_kernel<8>, grid, block, 0, st, xp, wp, op, rows, (int)hidden,
+                   x_row_stride, out_row_stride, eps);
   else if (vpl <= 12)
-    rms_norm_reg_kernel<12><<<grid, block, 0, st>>>(xp, wp, op, rows, (int)hidden, x_row_stride,
-                                                     out_row_stride, eps);
+    e = launch_pdl(rms_norm_reg_kernel<12>, grid, block, 0, st, xp, wp, op, rows, (int)hidden,
+                   x_row_stride, out_row_stride, eps);
   else if (vpl <= 16)
-    rms_norm_reg_kernel<16><<<grid, block, 0, st>>>(xp, wp, op, rows, (int)hidden, x_row_stride,
-                                                     out_row_stride, eps);
+    e = launch_pdl(rms_norm_reg_kernel<16>, grid, block, 0, st, xp, wp, op, rows, (int)hidden,
+                   x_row_stride, out_row_stride, eps);
   else
-    rms_norm_kernel<<<grid, block, 0, st>>>(xp, wp, op, rows, (int)hidden, x_row_stride,
-                                            out_row_stride, eps);
-  cudaError_t e = cudaGetLastError();
+    e = launch_pdl(rms_norm_kernel, grid, block, 0, st, xp, wp, op, rows, (int)hidden, x_row_stride,
+                   out_row_stride, eps);
   if (e != cudaSuccess) return cuda_fail(e, "fi_rms_norm launch");
   return FI_OK;
 }

@@ -42,6 +42,8 @@ __device__ __forceinline__ __half rope_elem(float x, float partner_signed, __hal
 }
 
 __global__ void __launch_bounds__(256) rope_kv_write_kernel(const RopeArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t half_chunks = a.hd / 16;  // 8-dim chunks per half
   const int64_t heads = a.nq + 2 * a.nkv;
   const int64_t total = a.batch * a.seq * heads * half_chunks;
@@ -185,8 +187,8 @@ extern "C" int fi_rope_kv_write(const void* qkv, int64_t batch, int64_t seq, int
   int64_t blocks = (total + threads - 1) / threads;
   const int64_t cap = (int64_t)sm_count() * 32;
   if (blocks > cap) blocks = cap;
-  rope_kv_write_kernel<<<(unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(a);
-  cudaError_t e = cudaGetLastError();
+  const cudaError_t e = launch_pdl(rope_kv_write_kernel, dim3((unsigned)blocks), dim3(threads), 0,
+                                   static_cast<cudaStream_t>(stream), a);
   if (e != cudaSuccess) return cuda_fail(e, "fi_rope_kv_write launch");
   return FI_OK;
 }
