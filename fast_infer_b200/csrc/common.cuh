@@ -30,6 +30,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// Start of the dynamic shared memory rounded up to 1024 bytes (the 128-byte swizzle
+// atom). Derived from the __shared__ array by pointer arithmetic only, so every load
+// and store addressed through it stays a shared-space access (an integer round trip
+// would leave the compiler generic loads and stores).
+__device__ __forceinline__ uint8_t* smem_align1024(uint8_t* raw) {
+  return raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u);
+}
+
 __device__ __forceinline__ void set_error(int* err, int code) {
   if (err) atomicOr(err, code);
 }

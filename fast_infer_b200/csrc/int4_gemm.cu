@@ -12,7 +12,8 @@
 // exactly as the reference computes it; products and sums are fp32, output fp16.
 //
 // fi_int4_gemm (M <= 64) streams the 4-bit weights once from HBM:
-// * Persistent CTAs, one producer warp + 8 consumer warps. The producer streams
+// * Persistent CTAs of one or two groups of (one producer warp + 8 consumer warps)
+//   sharing x staged in shared memory. Each group's producer streams
 //   16-row x 512-byte weight tiles (1024 k) with TMA into a shared-memory ring (one
 //   3-D box of 4 x 128-byte chunks per tile, 128B-swizzled so the consumers' 16-byte
 //   reads are conflict-free); each consumer warp takes 128 k of every tile.
@@ -33,7 +34,7 @@
 
 namespace fi {
 
-constexpr int kI4Consumers = 8;                         // math warps
+constexpr int kI4Consumers = 8;                         // math warps of a group
 constexpr int kI4Threads = (kI4Consumers + 1) * 32;     // + one TMA producer warp
 constexpr int kI4Rows = 16;        // weight rows (output columns) per work item
 constexpr int kI4KIter = 128;      // k per consumer warp per round: 4 threads x 32 nibbles
@@ -46,6 +47,7 @@ constexpr int kI4StageBytes = kI4Rows * kI4RoundK / 2;  // 8 KB
 #endif
 constexpr int kI4Stages = FI_I4_STAGES;
 constexpr int kI4ScaleBytes = kI4Rows * (kI4RoundK / 128) * 2;  // 256: 16 rows x 8 fp16
+constexpr int kI4XBatch = 8;      // x chunks each thread loads at once when staging
 constexpr int kI4MaxM = 64;        // up to eight 8-token tiles
 constexpr int kI4ConsumerBar = 1;  // named barrier of the 256 consumer threads
 
@@ -60,6 +62,21 @@ struct I4Args {
   int tma_scales;             // 1: each round's 16 x 8 scales arrive by TMA with its weights
   int64_t xs0, ss0, ss1, cs0, cs1;
 };
+
+// Item epilogue buffer in shared memory: consumer warps x 8*NT tokens x 17 floats
+// (16 rows + 1 of padding).
+template <int NT>
+__host__ __device__ constexpr size_t i4_red_bytes() {
+  return (size_t)kI4Consumers * NT * 8 * (kI4Rows + 1) * 4;
+}
+
+// One group's shared memory: weight ring, scale ring, barriers, epilogue buffer,
+// rounded up to 1024 bytes so every group's ring keeps the swizzle alignment.
+template <int NT>
+__host__ __device__ constexpr size_t i4_group_bytes() {
+  return ((size_t)kI4Stages * (kI4StageBytes + kI4ScaleBytes) + 256 + i4_red_bytes<NT>() + 1023) /
+         1024 * 1024;
+}
 
 struct I4Bars {
   uint64_t full[kI4Stages], empty[kI4Stages];
@@ -139,26 +156,40 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, uin
 // kSmemX: x is staged once into shared memory (rows < M, each 8-group in the order
 // 0,4,1,5,2,6,3,7 that dequant_word_perm produces, zeros past K); otherwise x
 // fragments come from global memory in natural order and dequant_word is used.
+// G > 1: G groups (8 math warps + 1 producer warp each, own ring and item slots)
+// share one staged x, so 9-16 tokens get 16 math warps per SM where a second CTA's
+// copy of x would not fit.
 // Every mbarrier wait is bounded: after a timeout (FI_DEVERR_TIMEOUT) the waits are
 // skipped, the loops still run to the end and the producer lets its copies land.
 // Up to 8 tokens the kernel fits 56 registers, so up to 4 CTAs share an SM (the ring
 // and staged x then decide); larger token tiles run one CTA per SM.
-template <int NT, bool kSmemX>
-__global__ void __launch_bounds__(kI4Threads, NT == 1 ? 4 : 1)
+// Launched with programmatic dependent launch: the producer pulls its first ring of
+// weight tiles into L2 while the previous kernel finishes; every read of x, of the
+// scales and of the ring waits for it (grid_dep_wait).
+template <int NT, bool kSmemX, int G>
+__global__ void __launch_bounds__(G * kI4Threads, NT == 1 ? 32 / kI4Consumers : 1)
     int4_gemm_kernel(const __grid_constant__ CUtensorMap tm_w,
                      const __grid_constant__ CUtensorMap tm_s, const I4Args a) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
-  uint8_t* stages = smem;
+  uint8_t* smem = smem_align1024(smem_raw);
+  // G groups of (8 consumer warps + 1 producer warp), each with its own ring, share
+  // one staged copy of x: group grp owns warps [grp*9, grp*9 + 9).
+  const int warp_all = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = warp_all / (kI4Consumers + 1);
+  const int warp = warp_all - grp * (kI4Consumers + 1);  // warp within the group
+  const int tid = warp * 32 + lane;                       // thread within the group
+  uint8_t* stages = smem + grp * i4_group_bytes<NT>();
   uint8_t* sstages = stages + kI4Stages * kI4StageBytes;  // kI4Stages x 256-byte scale tiles
   I4Bars* bars = reinterpret_cast<I4Bars*>(sstages + kI4Stages * kI4ScaleBytes);
-  __half* xs = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(bars) + 256);
-  __shared__ float red[kI4Consumers][NT * 8][kI4Rows + 1];
+  // partial sums of the item epilogue: [warp][token][row], rows padded to 17
+  auto red = reinterpret_cast<float(*)[NT * 8][kI4Rows + 1]>(reinterpret_cast<uint8_t*>(bars) + 256);
+  __half* xs = reinterpret_cast<__half*>(smem + G * i4_group_bytes<NT>());
+  const int group_bar = kI4ConsumerBar + grp;  // named barrier of this group's consumers
 
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // Item slots: slot grp of CTA b is b*G + grp; it takes items slot, slot + grid*G, ...
   const int items = (a.N + kI4Rows - 1) / kI4Rows;
-  const int my_items = blockIdx.x < items ? (items - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  const int slot = blockIdx.x * G + grp, nslots = gridDim.x * G;
+  const int my_items = slot < items ? (items - slot + nslots - 1) / nslots : 0;
   const int total = my_items * a.rounds;
 
   if (tid == 0) {
@@ -182,7 +213,7 @@ __global__ void __launch_bounds__(kI4Threads, NT == 1 ? 4 : 1)
       // written these weights), the first ring's worth of weight tiles only goes to
       // L2; the shared-memory copies start after grid_dep_wait().
       for (int q = 0; q < total && q < kI4Stages; ++q) {
-        const int item = blockIdx.x + (q / a.rounds) * gridDim.x, r = q % a.rounds;
+        const int item = slot + (q / a.rounds) * nslots, r = q % a.rounds;
         if (a.tma3d) {
           tma_prefetch_l2_3d(&tm_w, 0, item * kI4Rows, r * kI4Boxes);
         } else {
@@ -197,7 +228,7 @@ __global__ void __launch_bounds__(kI4Threads, NT == 1 ? 4 : 1)
         const int st = q % kI4Stages;
         if (q >= kI4Stages && !dead)
           dead = !mbar_wait(&bars->empty[st], ((q / kI4Stages) - 1) & 1, a.err);
-        const int item = blockIdx.x + (q / a.rounds) * gridDim.x, r = q % a.rounds;
+        const int item = slot + (q / a.rounds) * nslots, r = q % a.rounds;
         mbar_arrive_expect_tx(&bars->full[st],
                               kI4StageBytes + (a.tma_scales ? kI4ScaleBytes : 0));
         if (a.tma_scales)  // scales [N, K/128] fp16: 8 groups x 16 rows
@@ -225,23 +256,45 @@ __global__ void __launch_bounds__(kI4Threads, NT == 1 ? 4 : 1)
   grid_dep_wait();  // x and the scales may be the previous kernel's output
   const int g = lane >> 2, t = lane & 3;
   if constexpr (kSmemX) {
+    // Each thread owns chunk columns c (8 k each) and walks the token rows kXB at a
+    // time, with kXB independent 16-byte loads in flight: staging costs a few memory
+    // latencies, not one per chunk, and no index division (one token keeps a batch
+    // of one in the 56-register one-tile instance).
+    constexpr int kXB = NT == 1 ? 1 : kI4XBatch;
+    constexpr int kStride = G * kI4Consumers * 32;
     const int chunks = a.rounds * (kI4RoundK / 8);
     const int kchunks = a.K / 8;
-    for (int i = tid; i < a.M * chunks; i += kI4Consumers * 32) {
-      const int m = i / chunks, c = i - m * chunks;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (c < kchunks) {
-        const uint4 u = *reinterpret_cast<const uint4*>(a.x + m * a.xs0 + c * 8);
-        v = make_uint4(__byte_perm(u.x, u.z, 0x5410), __byte_perm(u.x, u.z, 0x7632),
-                       __byte_perm(u.y, u.w, 0x5410), __byte_perm(u.y, u.w, 0x7632));
-      }
-      *reinterpret_cast<uint4*>(xs + m * a.xstride + c * 8) = v;
-    }
-    named_bar_sync(kI4ConsumerBar, kI4Consumers * 32);
-  }
-  bool xv[NT];  // token nt*8 + g exists
+    for (int c = grp * kI4Consumers * 32 + tid; c < chunks; c += kStride) {
+      const __half* xc = a.x + c * 8;
+      __half* sc = xs + c * 8;
+      for (int m0 = 0; m0 < a.M; m0 += kXB) {
+        uint4 u[kXB];
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) xv[nt] = nt * 8 + g < a.M;
+        for (int j = 0; j < kXB; ++j) {
+          u[j] = make_uint4(0u, 0u, 0u, 0u);
+          if (m0 + j < a.M && c < kchunks)
+            u[j] = *reinterpret_cast<const uint4*>(xc + (int64_t)(m0 + j) * a.xs0);
+        }
+#pragma unroll
+        for (int j = 0; j < kXB; ++j) {
+          if (m0 + j >= a.M) break;
+          *reinterpret_cast<uint4*>(sc + (m0 + j) * a.xstride) = make_uint4(
+              __byte_perm(u[j].x, u[j].z, 0x5410), __byte_perm(u[j].x, u[j].z, 0x7632),
+              __byte_perm(u[j].y, u[j].w, 0x5410), __byte_perm(u[j].y, u[j].w, 0x7632));
+        }
+      }
+    }
+    named_bar_sync(kI4ConsumerBar + G, G * kI4Consumers * 32);  // every group's consumers
+  }
+  // Element offset of this lane's x row (token nt*8 + g) in xs or x. Tokens past M
+  // (padding of the last 8-token tile) read row M-1: their MMA columns are computed
+  // and never stored, so the loads need no predicate and no zero fill.
+  int64_t xo[NT];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int tok = min(nt * 8 + g, a.M - 1);
+    xo[nt] = kSmemX ? (int64_t)tok * a.xstride : (int64_t)tok * a.xs0;
+  }
 
   // scale of (row, k) for this lane; fetched one round ahead
   auto scale_of = [&](int item, int r, int h) -> uint16_t {
@@ -253,8 +306,8 @@ __global__ void __launch_bounds__(kI4Threads, NT == 1 ? 4 : 1)
   };
   uint16_t sa_n = 0, sb_n = 0;
   if (total > 0 && !a.tma_scales) {
-    sa_n = scale_of(blockIdx.x, 0, 0);
-    sb_n = scale_of(blockIdx.x, 0, 1);
+    sa_n = scale_of(slot, 0, 0);
+    sb_n = scale_of(slot, 0, 1);
   }
 
   float acc[NT][4];
@@ -269,12 +322,12 @@ __global__ void __launch_bounds__(kI4Threads, NT == 1 ? 4 : 1)
   const int swz = (chunk ^ g) << 4;          // 128B swizzle: chunk ^ (row % 8), row = g or g+8
   int q = 0;
   for (int j = 0; j < my_items; ++j) {
-    const int item = blockIdx.x + j * gridDim.x;
+    const int item = slot + j * nslots;
     for (int r = 0; r < a.rounds; ++r, ++q) {
       uint32_t s2a = splat16(sa_n), s2b = splat16(sb_n);
       if (!a.tma_scales) {  // prefetch the next round's scales
         const int r1 = r + 1 < a.rounds ? r + 1 : 0;
-        const int it1 = r + 1 < a.rounds ? item : item + gridDim.x;
+        const int it1 = r + 1 < a.rounds ? item : item + nslots;
         const bool more = q + 1 < total;
         sa_n = more ? scale_of(it1, r1, 0) : 0;
         sb_n = more ? scale_of(it1, r1, 1) : 0;
@@ -284,10 +337,10 @@ __global__ void __launch_bounds__(kI4Threads, NT == 1 ? 4 : 1)
       const uint8_t* sbase = stages + st * kI4StageBytes + box * (kI4Rows * kI4BoxBytes);
       const uint4 qa4 = *reinterpret_cast<const uint4*>(sbase + g * kI4BoxBytes + swz);
       const uint4 qb4 = *reinterpret_cast<const uint4*>(sbase + (g + 8) * kI4BoxBytes + swz);
-      if (a.tma_scales) {  // [16 rows][8 groups]: this warp's group is `warp`
+      if (a.tma_scales) {  // [16 rows][groups of the round]: this warp's group is `warp`
         const uint16_t* sc = reinterpret_cast<const uint16_t*>(sstages + st * kI4ScaleBytes);
-        s2a = splat16(sc[g * 8 + warp]);
-        s2b = splat16(sc[(g + 8) * 8 + warp]);
+        s2a = splat16(sc[g * (kI4RoundK / 128) + warp]);
+        s2b = splat16(sc[(g + 8) * (kI4RoundK / 128) + warp]);
       }
       // The stage is released before these values are used, and the next write to it
       // is a TMA (async proxy) write: order this thread's generic reads before it.
@@ -310,13 +363,12 @@ __global__ void __launch_bounds__(kI4Threads, NT == 1 ? 4 : 1)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           // B = x^T: token nt*8 + g, this lane's 8 k (pair order matching ba/bb)
-          uint4 u = make_uint4(0u, 0u, 0u, 0u);
-          const int tok = nt * 8 + g;
+          uint4 u;
           if constexpr (kSmemX) {
-            if (xv[nt]) u = *reinterpret_cast<const uint4*>(xs + tok * a.xstride + kk + 8 * wd);
+            u = *reinterpret_cast<const uint4*>(xs + xo[nt] + kk + 8 * wd);
           } else {
-            if (xv[nt] && kval)
-              u = __ldg(reinterpret_cast<const uint4*>(a.x + tok * a.xs0 + kk + 8 * wd));
+            u = make_uint4(0u, 0u, 0u, 0u);
+            if (kval) u = __ldg(reinterpret_cast<const uint4*>(a.x + xo[nt] + kk + 8 * wd));
           }
           // A = weights: rows g (ba) and g+8 (bb), two k pairs each
           mma_16816(acc[nt], ba[0], bb[0], ba[1], bb[1], u.x, u.y);
@@ -333,7 +385,7 @@ __global__ void __launch_bounds__(kI4Threads, NT == 1 ? 4 : 1)
         red[warp][nt * 8 + 2 * t + (e & 1)][g + (e >> 1) * 8] = acc[nt][e];
         acc[nt][e] = 0.f;
       }
-    named_bar_sync(kI4ConsumerBar, kI4Consumers * 32);
+    named_bar_sync(group_bar, kI4Consumers * 32);
     const int nbase = item * kI4Rows;
     for (int i = tid; i < a.M * kI4Rows; i += kI4Consumers * 32) {
       const int m = i / kI4Rows, rr = i - m * kI4Rows, n = nbase + rr;
@@ -342,7 +394,7 @@ __global__ void __launch_bounds__(kI4Threads, NT == 1 ? 4 : 1)
       for (int w = 0; w < kI4Consumers; ++w) sum += red[w][m][rr];
       if (n < a.N) a.c[m * a.cs0 + n * a.cs1] = __float2half_rn(sum);
     }
-    named_bar_sync(kI4ConsumerBar, kI4Consumers * 32);
+    named_bar_sync(group_bar, kI4Consumers * 32);
   }
 }
 
@@ -365,28 +417,27 @@ __global__ void __launch_bounds__(256) int4_dequant_kernel(const uint8_t* w, con
 }
 
 constexpr size_t kI4SmemOptin = 232448;  // per-block shared memory limit (227 KB)
-constexpr size_t kI4SmemFixed =
-    1024 + (size_t)kI4Stages * (kI4StageBytes + kI4ScaleBytes) + 256;
 
-// Largest staged x for an instance: the limit minus the ring, the barriers and the
-// static reduction buffer (8 warps x 8*NT tokens x 17 floats), less 1 KB of margin.
+// Dynamic shared memory without x: 1 KB of alignment slack and G groups.
+template <int NT, int G>
+constexpr size_t i4_smem_base() {
+  return 1024 + (size_t)G * i4_group_bytes<NT>();
+}
+
+// Largest staged x for an instance: the limit minus the groups, less 1 KB of margin.
 #ifndef FI_I4_XMAX_KB
 #define FI_I4_XMAX_KB 1024
 #endif
-template <int NT>
+template <int NT, int G>
 constexpr size_t i4_smem_x_max() {
-  constexpr size_t fit =
-      kI4SmemOptin - kI4SmemFixed - (size_t)kI4Consumers * NT * 8 * (kI4Rows + 1) * 4 - 1024;
+  constexpr size_t used = i4_smem_base<NT, G>() + 1024;
+  constexpr size_t fit = used < kI4SmemOptin ? kI4SmemOptin - used : 0;
   return fit < (size_t)FI_I4_XMAX_KB * 1024 ? fit : (size_t)FI_I4_XMAX_KB * 1024;
-}
-
-static size_t i4_smem_bytes(bool smem_x, const I4Args& a) {
-  return kI4SmemFixed + (smem_x ? (size_t)a.M * (size_t)a.xstride * 2 : 0);
 }
 
 // Opts each instance in to its largest shared-memory layout (once per device), sizes
 // the persistent grid with the occupancy calculator for this call's layout, launches.
-template <int NT, bool kSmemX>
+template <int NT, bool kSmemX, int G>
 static int launch_int4_gemm(cudaStream_t st, const CUtensorMap& tm, const CUtensorMap& tms,
                             const I4Args& a) {
   static bool attr_done[64] = {false};
@@ -394,32 +445,40 @@ static int launch_int4_gemm(cudaStream_t st, const CUtensorMap& tm, const CUtens
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
   if (!attr_done[dev]) {
-    const int max_smem = (int)(kI4SmemFixed + (kSmemX ? i4_smem_x_max<NT>() : 0));
-    cudaError_t e = cudaFuncSetAttribute(int4_gemm_kernel<NT, kSmemX>,
+    const int max_smem = (int)(i4_smem_base<NT, G>() + (kSmemX ? i4_smem_x_max<NT, G>() : 0));
+    cudaError_t e = cudaFuncSetAttribute(int4_gemm_kernel<NT, kSmemX, G>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
     if (e != cudaSuccess) return cuda_fail(e, "fi_int4_gemm: cudaFuncSetAttribute");
     attr_done[dev] = true;
   }
-  const size_t smem = i4_smem_bytes(kSmemX, a);
+  const size_t smem =
+      i4_smem_base<NT, G>() + (kSmemX ? (size_t)a.M * (size_t)a.xstride * 2 : 0);
+  const int threads = G * kI4Threads;
   int nb = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, int4_gemm_kernel<NT, kSmemX>,
-                                                    kI4Threads, smem) != cudaSuccess || nb < 1)
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, int4_gemm_kernel<NT, kSmemX, G>,
+                                                    threads, smem) != cudaSuccess || nb < 1)
     nb = 1;
   const int items = (a.N + kI4Rows - 1) / kI4Rows;
   int grid = nb * sm_count();
-  if (grid > items) grid = items;
-  cudaError_t e = launch_pdl(int4_gemm_kernel<NT, kSmemX>, dim3((unsigned)grid), dim3(kI4Threads),
-                             smem, st, tm, tms, a);
+  if (grid > (items + G - 1) / G) grid = (items + G - 1) / G;
+  cudaError_t e = launch_pdl(int4_gemm_kernel<NT, kSmemX, G>, dim3((unsigned)grid),
+                             dim3(threads), smem, st, tm, tms, a);
   if (e != cudaSuccess) return cuda_fail(e, "fi_int4_gemm launch");
   return FI_OK;
 }
 
+// x staged in shared memory when it fits; for two 8-token tiles (9-16 tokens) two
+// groups share one staged x when both rings fit beside it (16 math warps per SM).
 template <int NT>
 static int launch_int4_gemm_nt(cudaStream_t st, const CUtensorMap& tm, const CUtensorMap& tms,
                                const I4Args& a) {
-  if ((size_t)a.M * (size_t)a.xstride * 2 <= i4_smem_x_max<NT>())
-    return launch_int4_gemm<NT, true>(st, tm, tms, a);
-  return launch_int4_gemm<NT, false>(st, tm, tms, a);
+  const size_t xbytes = (size_t)a.M * (size_t)a.xstride * 2;
+  if constexpr (NT == 2) {
+    if (xbytes <= i4_smem_x_max<NT, 2>())
+      return launch_int4_gemm<NT, true, 2>(st, tm, tms, a);
+  }
+  if (xbytes <= i4_smem_x_max<NT, 1>()) return launch_int4_gemm<NT, true, 1>(st, tm, tms, a);
+  return launch_int4_gemm<NT, false, 1>(st, tm, tms, a);
 }
 
 }  // namespace fi

@@ -82,8 +82,7 @@ __global__ void __launch_bounds__(kDecThreads, 2)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const DecodeParams p) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  uint8_t* smem = smem_align1024(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDecStages * kStageBytes);
   uint64_t* empty = full + kDecStages;
   int* s_phys = reinterpret_cast<int*>(empty + kDecStages);

@@ -167,8 +167,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                        const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v, const PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  uint8_t* smem = smem_align1024(smem_raw);
   uint8_t* sQ = smem;                                  // 2 tiles
   uint8_t* sK = smem + 2 * kTileBytes;                 // kPfStages tiles
   uint8_t* sV = sK + kPfStages * kTileBytes;           // kPfStages tiles
