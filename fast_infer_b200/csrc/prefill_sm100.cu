@@ -161,6 +161,36 @@ __device__ __forceinline__ void tma_tile_half(void* dst, const CUtensorMap* m, u
     tma_load_4d(dst, m, bar, d0, row, h, u.b);
 }
 
+// One pass of the online softmax over a row of S held in registers (one thread =
+// one row): p = 2^(s*sl2 - mref) with the scaling on packed FFMA2 and exp2 on MUFU
+// (and, for kEmuPairsPer8 of every 8 column pairs, on the FMA pipe); the row sum in 4
+// packed FADD2 chains; P packed to fp16 in place (entry c/2 written after entries c
+// and c+1 were read).
+__device__ __forceinline__ void softmax_pass(uint32_t* sr, float sl2, float mref, float& lsum) {
+  const uint64_t sc2 = f32x2(sl2, sl2), nm2 = f32x2(-mref, -mref);
+  uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+  for (int c = 0; c < kBN; c += 2) {
+    const uint64_t xp =
+        fma_f32x2(f32x2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), sc2, nm2);
+    float p0, p1;
+    if (((c >> 1) & 7) < kEmuPairsPer8) {
+      exp2_poly_x2(xp, p0, p1);
+    } else {
+      float x0, x1;
+      f32x2_split(xp, x0, x1);
+      p0 = fast_exp2(x0);
+      p1 = fast_exp2(x1);
+    }
+    sum2[(c >> 1) & 3] = add_f32x2(sum2[(c >> 1) & 3], f32x2(p0, p1));
+    sr[c >> 1] = pack_half2(p0, p1);
+  }
+  const uint64_t s01 = add_f32x2(add_f32x2(sum2[0], sum2[1]), add_f32x2(sum2[2], sum2[3]));
+  float lo, hi;
+  f32x2_split(s01, lo, hi);
+  lsum = lo + hi;
+}
+
 template <bool kPacked>
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -379,6 +409,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           for (int c = 0; c < kBN; ++c)
             if (c > row) sr[c] = __float_as_uint(-INFINITY);
         }
+        // Lazy rescale: only rows whose max grew by more than the threshold move
+        // their reference point (and then O_t and l are rescaled by alpha).
+        bool rescale = false;
+        float alpha = 1.f, lt;
         // Row max as 8 independent chains of 3-input max (short dependency chains).
         float mx8[8];
 #pragma unroll
@@ -391,12 +425,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
         const float mx = fmaxf(fmax3f(mx8[0], mx8[1], mx8[2]),
                                fmax3f(fmax3f(mx8[3], mx8[4], mx8[5]), mx8[6], mx8[7]));
-        const float m_tile = mx * sl2;
-        const float m_new = fmaxf(m, m_tile);
-        // Lazy rescale: only rows whose max grew by more than the threshold move
-        // their reference point (and then O_t and l are rescaled by alpha).
-        bool rescale = false;
-        float alpha = 1.f;
+        const float m_new = fmaxf(m, mx * sl2);
         if (j == 0) {
           m = m_new;
         } else {
@@ -408,35 +437,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             l *= alpha;
           }
         }
-        const float mref = (m == -INFINITY) ? 0.f : m;
-        // p = 2^(s*scale_log2 - m): scaling on packed FFMA2, exp2 on MUFU (and on the
-        // FMA pipe for a share of the columns), row sum in 4 packed FADD2 chains;
-        // P packed in place (entry c/2 written after entries c and c+1 were read).
-        const uint64_t sc2 = f32x2(sl2, sl2), nm2 = f32x2(-mref, -mref);
-        uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
-#pragma unroll
-        for (int c = 0; c < kBN; c += 2) {
-          const uint64_t xp =
-              fma_f32x2(f32x2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), sc2, nm2);
-          float p0, p1;
-          if (((c >> 1) & 7) < kEmuPairsPer8) {
-            exp2_poly_x2(xp, p0, p1);
-          } else {
-            float x0, x1;
-            f32x2_split(xp, x0, x1);
-            p0 = fast_exp2(x0);
-            p1 = fast_exp2(x1);
-          }
-          sum2[(c >> 1) & 3] = add_f32x2(sum2[(c >> 1) & 3], f32x2(p0, p1));
-          sr[c >> 1] = pack_half2(p0, p1);
-        }
-        {
-          const uint64_t s01 =
-              add_f32x2(add_f32x2(sum2[0], sum2[1]), add_f32x2(sum2[2], sum2[3]));
-          float lo, hi;
-          f32x2_split(s01, lo, hi);
-          l += lo + hi;
-        }
+        softmax_pass(sr, sl2, (m == -INFINITY) ? 0.f : m, lt);
+        l += lt;
         tmem_st32(tS + 0, sr);
         tmem_st32(tS + 32, sr + 32);
         if (rescale) {
