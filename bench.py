@@ -389,6 +389,7 @@ def run_ours(args):
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline_decode(wl.lens, threads=1)
+        result["prefill"]["cpu_baseline"] = cpu_baseline_prefill()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -648,6 +649,31 @@ def cpu_baseline_decode(lens, threads=1, budget_s=12.0):
             "kind": "port",
             "sample": f"{used} of {n} sequences of the decode workload (one layer), numpy "
                       f"oracle paged_attention_vectorized, {secs:.1f} s"}
+
+
+def cpu_baseline_prefill(reps=2):
+    """The CPU equivalent of the prefill on the host cores: fp32 causal attention with
+    GQA through PyTorch's scaled_dot_product_attention (all threads) on the whole
+    config-2 shape; best of ``reps``, TFLOP/s of the exact causal count."""
+    import torch
+    ncores = os.cpu_count() or 1
+    torch.set_num_threads(ncores)
+    g = torch.Generator().manual_seed(PF_SEED)
+    q = torch.randn(PF_B, HQ, PF_S, D, generator=g)
+    k = torch.randn(PF_B, HKV, PF_S, D, generator=g)
+    v = torch.randn(PF_B, HKV, PF_S, D, generator=g)
+    best = float("inf")
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True,
+                                                         enable_gqa=True)
+        best = min(best, time.perf_counter() - t0)
+    flops = PF_B * HQ * 4.0 * D * PF_S * (PF_S + 1) / 2.0
+    return {"value": round(flops / best / 1e12, 4), "unit": "TFLOP/s", "cores": ncores,
+            "kind": "port",
+            "sample": f"whole config-2 prefill (B4 x S2048, 24/8 heads), fp32 PyTorch "
+                      f"scaled_dot_product_attention(is_causal, enable_gqa) on the CPU, "
+                      f"best of {reps}: {best:.2f} s"}
 
 
 def _ref_inputs(idx):
