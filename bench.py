@@ -511,13 +511,14 @@ def run_stack(torch, dev, rank, world, dist, warmup=1):
     torch.cuda.synchronize()
     dec_ms = max_ms(e[0].elapsed_time(e[1]))
     finite = bool(torch.isfinite(h).all().item())
-    st.release_graph()
+    st.close()
     sync_all()
     return {
         "workload": "config 4: 28-layer attention stack (Llama-3.2-3B attention shapes, random "
                     "weights), B16, prefill 1024 then 256 decode steps, KV heads sharded over "
-                    f"{world} GPU(s), NCCL all-gather of head outputs per layer; prefill = median "
-                    "of 3 timed passes",
+                    f"{world} GPU(s), head outputs all-gathered per layer (decode: one "
+                    "peer-memory kernel over NVLink; prefill: NCCL); prefill = median of 3 "
+                    "timed passes",
         "scaling": "strong",
         "prefill_ms": round(pf_ms, 3),
         "prefill_tokens_per_s": round(STACK_BATCH * STACK_PROMPT / (pf_ms * 1e-3), 1),

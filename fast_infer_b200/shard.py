@@ -12,7 +12,9 @@ with no collective on the data path, one process per GPU:
 The only collective is ``gather_heads``: where a caller needs the attention output
 whole (the O projection of a tensor-parallel-free layer), the per-rank
 [tokens, heads_r*D] outputs are all-gathered (NCCL over NVLink on B200; gloo in the
-CPU tests) and reassembled in head order.
+CPU tests) and reassembled in head order. ``PeerGather`` does the same for the
+decode step in one kernel of our own: each rank stores its rows straight into every
+rank's buffer over NVLink (CUDA IPC mappings) and waits on per-call flags.
 """
 
 from __future__ import annotations
@@ -80,6 +82,107 @@ def gather_heads(local, group=None, head_dim_axis: int = -1):
     if world == 1:
         return local
     local = local.contiguous()
+    if dist.get_backend(group) == "nccl" and head_dim_axis in (-1, local.dim() - 1):
+        # one collective into [world, ...], then one copy into head order
+        out = torch.empty((world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
+        dist.all_gather_into_tensor(out, local, group=group)
+        return out.movedim(0, -2).reshape(*local.shape[:-1], world * local.shape[-1])
     parts = [torch.empty_like(local) for _ in range(world)]
     dist.all_gather(parts, local, group=group)
     return torch.cat(parts, dim=head_dim_axis)
+
+
+class _DeviceArray:
+    """Zero-copy view of raw device memory for torch.as_tensor."""
+
+    def __init__(self, ptr: int, shape, typestr: str = "<f2"):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (ptr, False), "version": 3}
+
+
+class PeerGather:
+    """``gather_heads`` for the decode step, over NVLink peer memory instead of NCCL.
+
+    Every rank allocates one region of ``nbuf`` gather buffers [max_rows, world *
+    row_elems] fp16 and maps every other rank's region (CUDA IPC handles exchanged
+    with ``all_gather_object`` on ``group``). ``gather(local, buffer)`` is one kernel
+    (``fi_peer_gather``) that stores this rank's rows into buffer ``buffer`` of every
+    region and waits until every rank has delivered the same call; it returns this
+    rank's buffer as [rows, world * row_elems], heads in their original order. Every
+    rank must make the same sequence of calls, and two uses of one buffer need another
+    gather between them (the stack uses one buffer per layer). Construct it on every
+    rank at the same point (it runs collectives); call ``close`` before the process
+    group goes away.
+    """
+
+    def __init__(self, max_rows: int, row_elems: int, nbuf: int, group=None, device=None):
+        import ctypes
+        import torch
+        import torch.distributed as dist
+        from fast_infer_b200 import _lib
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("PeerGather supports up to 8 ranks")
+        self.device = torch.device(device or "cuda")
+        self.max_rows, self.row_elems, self.nbuf = max_rows, row_elems, nbuf
+        self._lib = lib = _lib.load()
+        row_total = self.world * row_elems * 2
+        nbytes = lib.fi_peer_gather_bytes(nbuf, max_rows, row_total)
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * 64)()
+        with torch.cuda.device(self.device):
+            _lib.check(lib.fi_peer_alloc(nbytes, ctypes.byref(own), handle), "fi_peer_alloc")
+        self._own = own.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._opened = []
+        bases = []
+        with torch.cuda.device(self.device):
+            for p, hb in enumerate(handles):
+                if p == self.rank:
+                    bases.append(self._own)
+                    continue
+                ptr = ctypes.c_void_p()
+                hbuf = (ctypes.c_uint8 * 64).from_buffer_copy(hb)
+                _lib.check(lib.fi_peer_open(hbuf, ctypes.byref(ptr)), "fi_peer_open")
+                self._opened.append(ptr.value)
+                bases.append(ptr.value)
+        self._bases = (ctypes.c_void_p * 8)(*bases, *([None] * (8 - self.world)))
+        self._buffers = torch.as_tensor(
+            _DeviceArray(self._own, (nbuf, max_rows, self.world * row_elems)), device=self.device)
+
+    def gather(self, local, buffer: int):
+        import ctypes
+        from fast_infer_b200 import _lib
+        from fast_infer_b200._runtime import device_errors, error_word, stream_of
+        rows = local.numel() // self.row_elems
+        x = local.reshape(rows, self.row_elems)
+        if x.stride(1) != 1 or (x.stride(0) * 2) % 16 != 0 or x.data_ptr() % 16 != 0:
+            x = x.contiguous()
+        err = error_word(self.device)
+        st = self._lib.fi_peer_gather(
+            x.data_ptr(), rows, self.row_elems * 2, x.stride(0) * 2,
+            ctypes.cast(self._bases, ctypes.POINTER(ctypes.c_void_p)), self.world, self.rank,
+            buffer, self.nbuf, self.max_rows, err.data_ptr() if err is not None else None,
+            stream_of(self.device))
+        _lib.check(st, "peer gather")
+        device_errors(err, "peer gather")
+        return self._buffers[buffer, :rows].view(*local.shape[:-1], self.world * self.row_elems)
+
+    def close(self, group=None):
+        """Unmap the peers' regions and free this rank's once every rank has unmapped
+        it (collective: every rank calls it)."""
+        import torch
+        import torch.distributed as dist
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                self._lib.fi_peer_close(p)
+            self._opened = []
+            self._buffers = None
+            dist.barrier(group=group)
+            self._lib.fi_peer_free(self._own)
+        self._own = None

@@ -28,6 +28,8 @@ below restate the reference's RoPE and RMSNorm in PyTorch for tests.
 
 from __future__ import annotations
 
+import os
+
 from typing import Callable, Optional
 
 import torch
@@ -36,7 +38,7 @@ from fast_infer_b200._runtime import device_checks
 from fast_infer_b200.kernels.attention import flash_attention, paged_attention
 from fast_infer_b200.kernels.rms_norm import rms_norm
 from fast_infer_b200.kv_cache import KVCache, rope_and_store
-from fast_infer_b200.shard import HeadShard, gather_heads, head_shard
+from fast_infer_b200.shard import HeadShard, PeerGather, gather_heads, head_shard
 
 
 def precompute_freqs(head_dim: int, max_seq_len: int, theta: float, device) -> tuple:
@@ -78,6 +80,11 @@ class AttentionStack:
         self.shard: HeadShard = head_shard(rank, world, num_q_heads, num_kv_heads)
         self.world = world
         self.gather = gather if gather is not None else gather_heads
+        # decode-step gather over NVLink peer memory (set up with the decode state on
+        # multi-rank CUDA runs that use the default gather; FI_P2P_GATHER=0 keeps NCCL)
+        self._peer = None
+        self._peer_wanted = (gather is None and world > 1 and num_layers >= 2 and
+                             os.environ.get("FI_P2P_GATHER", "1") != "0")
         g = torch.Generator(device=self.device)
         g.manual_seed(seed)
         dev = self.device
@@ -107,8 +114,12 @@ class AttentionStack:
         self.cache._grow_batch(self.batch)
         self.token_count = 0
 
-    def _gather(self, o: torch.Tensor) -> torch.Tensor:
-        return o if self.world == 1 else self.gather(o)
+    def _gather(self, o: torch.Tensor, layer: Optional[int] = None) -> torch.Tensor:
+        if self.world == 1:
+            return o
+        if layer is not None and self._peer is not None:
+            return self._peer.gather(o, layer)  # one buffer per layer
+        return self.gather(o)
 
     @staticmethod
     def _residual(h: torch.Tensor, o: torch.Tensor, wo: torch.Tensor) -> None:
@@ -158,6 +169,9 @@ class AttentionStack:
             self._ws = torch.empty(max(need, 1), dtype=torch.uint8, device=self.device)
             self._h_in = torch.zeros(B, 1, self.hidden, dtype=torch.float16, device=self.device)
             self._graph = None
+            if self._peer_wanted and self._peer is None:
+                self._peer = PeerGather(B, self.shard.num_q_heads * self.D, self.L,
+                                        device=self.device)
 
     def _decode_body(self):
         """One decode token through every layer, reading positions from device
@@ -172,7 +186,7 @@ class AttentionStack:
             o = paged_attention(q[:, 0], self.cache.k[li], self.cache.v[li],
                                 self.cache.block_table, 64, 0, context_lens=self._dev_ctx,
                                 max_context_len=span, workspace=self._ws)
-            o = self._gather(o.reshape(B, 1, nq * D))
+            o = self._gather(o.reshape(B, 1, nq * D), li)
             self._residual(h, o, w["wo"])
         self._dev_ctx.add_(1)
         self._dev_start.add_(1)
@@ -235,6 +249,14 @@ class AttentionStack:
         """Drop the captured decode graph (call before destroying a process group
         whose collectives it holds)."""
         self._graph = None
+
+    def close(self):
+        """Release the decode graph and the peer-memory gather buffers (collective on
+        multi-rank runs: every rank calls it before the process group goes away)."""
+        self.release_graph()
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
 
     def forward(self, h: torch.Tensor) -> torch.Tensor:
         """Reference-style entry (model.py:50-160): S > 1 or the first call = prefill,

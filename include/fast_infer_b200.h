@@ -6,7 +6,9 @@
  * outermost first), shapes, a softmax scale and a CUDA stream (cudaStream_t passed
  * as void*). Nothing here allocates, synchronises the stream or keeps global state:
  * calls are asynchronous on `stream`, re-entrant, and every buffer belongs to the
- * caller. Each call returns FI_OK or an FI_ERR_* code after validating its
+ * caller (the peer-gather set-up calls at the end are the exception: they allocate
+ * and map the shared regions once). Each call returns FI_OK or an FI_ERR_* code
+ * after validating its
  * arguments on the host; fi_last_error() then gives a one-line message
  * (thread-local).
  *
@@ -272,6 +274,35 @@ int fi_int4_dequant(const void* packed, const void* scales, void* out, int64_t n
 int fi_int4_quantize(const void* w, void* packed, void* scales, int64_t n, int64_t k,
                      int64_t groupsize, const int64_t* w_strides, const int64_t* packed_strides,
                      const int64_t* scales_strides, void* stream);
+
+/*
+ * Head-output all-gather over NVLink peer memory, for a stack sharded by KV head.
+ *
+ * Replaces: the NCCL all-gather of per-rank attention outputs [rows, heads_r * 128]
+ * before the replicated O projection (model.py:123-134 with the heads split over
+ * GPUs; the one exchange of the sharded path). Set-up (these allocate and
+ * synchronise; call once): every rank calls fi_peer_alloc for a region of
+ * fi_peer_gather_bytes(nbuf, max_rows, world * row_bytes) bytes and shares the
+ * 64-byte `handle` with the others (e.g. through torch.distributed), which map it
+ * with fi_peer_open. bases[p] is rank p's region as mapped on this rank
+ * (bases[rank] = this rank's own pointer).
+ *
+ * fi_peer_gather: writes src [rows, row_bytes] (16-byte aligned rows) into buffer
+ * `buffer` of every rank's region at [row, rank * row_bytes], then waits on the device
+ * until every rank has delivered the same call (bounded: FI_DEVERR_TIMEOUT after 2 s).
+ * On return of the kernel this rank's buffer holds [rows, world * row_bytes] with rank
+ * p's block at p. Calls are counted on the device, so a CUDA graph replays correctly;
+ * every rank must make the same sequence of calls, and two uses of one buffer need
+ * another gather between them. world <= 8.
+ */
+size_t fi_peer_gather_bytes(int64_t nbuf, int64_t max_rows, int64_t row_total_bytes);
+int fi_peer_alloc(size_t bytes, void** ptr, void* handle);
+int fi_peer_open(const void* handle, void** ptr);
+int fi_peer_close(void* ptr);
+int fi_peer_free(void* ptr);
+int fi_peer_gather(const void* src, int64_t rows, int64_t row_bytes, int64_t src_row_stride_bytes,
+                   void* const* bases, int64_t world, int64_t rank, int64_t buffer, int64_t nbuf,
+                   int64_t max_rows, int32_t* error_flag, void* stream);
 
 #ifdef __cplusplus
 }
