@@ -32,8 +32,9 @@ namespace fi {
 
 constexpr int kD = 128;
 constexpr int kPage = 64;
-constexpr int kDecWarps = 4;
-constexpr int kDecThreads = (kDecWarps + 1) * 32;
+constexpr int kDecWarps = 4;  // consumer warps of a page group (16 rows each)
+// Threads of a CTA whose kGrp groups of 4 consumer warps take alternate pages.
+__host__ __device__ constexpr int dec_threads(int kgrp) { return (kDecWarps * kgrp + 1) * 32; }
 #ifndef FI_DEC_STAGES
 #define FI_DEC_STAGES 3
 #endif
@@ -41,8 +42,11 @@ constexpr int kDecStages = FI_DEC_STAGES;
 constexpr int kRegionBytes = kPage * 64 * 2;    // 64 rows x 64 fp16
 constexpr int kStageBytes = 4 * kRegionBytes;   // K lo, K hi, V lo, V hi
 constexpr int kMaxPagesPerSplit = 32;
-constexpr int kDecSmemBytes =
-    1024 + kDecStages * kStageBytes + 2 * kDecStages * 8 + kMaxPagesPerSplit * 4;
+// Shared memory of a CTA with kgrp page groups, each with its own kDecStages ring.
+__host__ __device__ constexpr int dec_smem_bytes(int kgrp) {
+  return 1024 + kgrp * kDecStages * kStageBytes + 2 * kgrp * kDecStages * 8 +
+         kMaxPagesPerSplit * 4;
+}
 
 struct DecodeParams {
   const __half* q;
@@ -78,14 +82,25 @@ __device__ __forceinline__ uint32_t swz(uint32_t region, int row, int chunk) {
   return region + row * 128 + ((chunk ^ (row & 7)) << 4);
 }
 
-__global__ void __launch_bounds__(kDecThreads, 2)
+// kGrp = 2 (grids of at most one CTA per SM): two groups of four consumer warps take
+// alternate pages of the split, so a CTA has two pages in flight through its
+// per-page dependency chain (QK^T, softmax, PV) where one group would leave the SM
+// waiting; the groups' states merge with the warps' at the end. Each group has its
+// own ring (page i -> group i % kGrp, slot (i / kGrp) % kDecStages of that ring), so
+// every waiter is at most one mbarrier phase ahead: with one shared ring a group
+// could wait on a slot two phases ahead, and the parity test would report the
+// previous phase as the one it wants.
+template <int kGrp>
+__global__ void __launch_bounds__(dec_threads(kGrp), kGrp == 1 ? 2 : 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const DecodeParams p) {
+  constexpr int kCW = kDecWarps * kGrp;  // consumer warps
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDecStages * kStageBytes);
-  uint64_t* empty = full + kDecStages;
-  int* s_phys = reinterpret_cast<int*>(empty + kDecStages);
+  constexpr int kS = kGrp * kDecStages;  // ring slots of all groups
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kS * kStageBytes);
+  uint64_t* empty = full + kS;
+  int* s_phys = reinterpret_cast<int*>(empty + kS);
 
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -109,13 +124,13 @@ __global__ void __launch_bounds__(kDecThreads, 2)
   const int nsplits = (npages + p.pps - 1) / p.pps;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kDecStages; ++s) {
+    for (int s = 0; s < kS; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kDecWarps);
     }
     fence_barrier_init();
   }
-  if (warp == kDecWarps) {
+  if (warp == kCW) {
     for (int i = lane; i < n; i += 32) {
       int ph = p.bt[b * p.bts[0] + (int64_t)(pg0 + i) * p.bts[1]];
       if (ph < 0 || ph >= p.num_blocks) {
@@ -127,14 +142,15 @@ __global__ void __launch_bounds__(kDecThreads, 2)
   }
   __syncthreads();
 
-  if (warp == kDecWarps) {
+  if (warp == kCW) {
     // ------------------------------------------------------------- producer
     if (lane == 0) {
       prefetch_tmap(&tm_k);
       prefetch_tmap(&tm_v);
       for (int i = 0; i < n; ++i) {
-        const int s = i % kDecStages;
-        if (i >= kDecStages && !mbar_wait(&empty[s], ((i / kDecStages) - 1) & 1, p.err)) break;
+        const int j = i / kGrp;  // page index within its group
+        const int s = (i % kGrp) * kDecStages + j % kDecStages;
+        if (j >= kDecStages && !mbar_wait(&empty[s], ((j / kDecStages) - 1) & 1, p.err)) break;
         const int ph = s_phys[i];
         if (ph < 0) {
           mbar_arrive(&full[s]);
@@ -177,12 +193,13 @@ __global__ void __launch_bounds__(kDecThreads, 2)
   float acc[8][4];
 #pragma unroll
   for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
-  const int row_base = warp * 16;
+  const int row_base = (warp % kDecWarps) * 16;
   bool aborted = false;
 
-  for (int i = 0; i < n; ++i) {
-    const int s = i % kDecStages;
-    if (!mbar_wait(&full[s], (i / kDecStages) & 1, p.err)) {
+  for (int i = warp / kDecWarps; i < n; i += kGrp) {
+    const int j = i / kGrp;  // page index within this group
+    const int s = (i % kGrp) * kDecStages + j % kDecStages;
+    if (!mbar_wait(&full[s], (j / kDecStages) & 1, p.err)) {
       aborted = true;
       break;
     }
@@ -265,9 +282,9 @@ __global__ void __launch_bounds__(kDecThreads, 2)
 
   // ------------------------------------------------ merge the four warps' state
   __syncthreads();  // every page consumed, every TMA landed: the ring is free
-  float* s_acc = reinterpret_cast<float*>(smem);            // [4 warps][8 heads][128]
-  float* s_m = s_acc + kDecWarps * 8 * kD;                   // [4][8]
-  float* s_l = s_m + kDecWarps * 8;                          // [4][8]
+  float* s_acc = reinterpret_cast<float*>(smem);            // [kCW warps][8 heads][128]
+  float* s_m = s_acc + kCW * 8 * kD;                         // [kCW][8]
+  float* s_l = s_m + kCW * 8;                                // [kCW][8]
   {
     float* wa = s_acc + warp * 8 * kD;
     const int h0 = 2 * tq, h1 = 2 * tq + 1;
@@ -286,8 +303,8 @@ __global__ void __launch_bounds__(kDecThreads, 2)
       s_l[warp * 8 + h1] = l1;
     }
   }
-  named_bar_sync(1, kDecWarps * 32);
-  if (aborted) return;
+  named_bar_sync(1, kCW * 32);
+  if (aborted || threadIdx.x >= kDecWarps * 32) return;
   {
     const int t = threadIdx.x;            // 0..127
     const int h = t >> 4;                 // head slot 0..7
@@ -295,13 +312,13 @@ __global__ void __launch_bounds__(kDecThreads, 2)
     if (h < p.group) {
       float M = -INFINITY;
 #pragma unroll
-      for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, s_m[w * 8 + h]);
+      for (int w = 0; w < kCW; ++w) M = fmaxf(M, s_m[w * 8 + h]);
       float L = 0.f, o[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) o[e] = 0.f;
       if (M != -INFINITY) {
 #pragma unroll
-        for (int w = 0; w < kDecWarps; ++w) {
+        for (int w = 0; w < kCW; ++w) {
           const float wt = fast_exp2(s_m[w * 8 + h] - M);
           L += s_l[w * 8 + h] * wt;
           const float* src = s_acc + (w * 8 + h) * kD + d0;
@@ -382,14 +399,12 @@ __global__ void __launch_bounds__(128) paged_decode_combine_kernel(const DecodeP
 static int choose_pps(int64_t batch, int64_t hkv, int64_t max_pages, int64_t requested) {
   if (requested > 0) return (int)(requested < kMaxPagesPerSplit ? requested : kMaxPagesPerSplit);
   const int64_t units = batch * hkv > 0 ? batch * hkv : 1;
-  // One CTA per (sequence, KV head) already filling most SMs beats any split: the
-  // combine launch and the partials cost more than the extra parallelism buys
-  // (batch 16 / 32 / 64 x 8 KV heads measured fastest unsplit). Below that, aim at
-  // about two CTAs per SM.
-  if (units * 4 >= (int64_t)sm_count() * 3) return kMaxPagesPerSplit;
-  const int64_t target = (int64_t)sm_count() * 2;
-  int64_t splits = (target + units - 1) / units;
-  if (splits < 1) splits = 1;
+  // Small grids run one CTA per SM with two page groups; measured on B200 the best
+  // split gives about half the SMs such a CTA (B=1..16 x 1..8 KV heads, 1K-8K
+  // tokens: within 7 % of the best of pages_per_split 4..32). Unsplit once one CTA
+  // per (sequence, KV head) reaches that (32 pages per CTA at most).
+  const int64_t splits = (int64_t)sm_count() / (2 * units);
+  if (splits <= 1) return kMaxPagesPerSplit;
   int64_t pps = (max_pages + splits - 1) / splits;
   if (pps < 4) pps = 4;
   if (pps > kMaxPagesPerSplit) pps = kMaxPagesPerSplit;
@@ -518,14 +533,22 @@ extern "C" int fi_paged_decode(const void* q, const void* k_cache, const void* v
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(paged_decode_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(
+        paged_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, dec_smem_bytes(1));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(paged_decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               dec_smem_bytes(2));
     if (e != cudaSuccess) return cuda_fail(e, "fi_paged_decode: cudaFuncSetAttribute");
     attr_done[dev] = true;
   }
   dim3 grid((unsigned)max_splits, (unsigned)num_kv_heads, (unsigned)batch);
-  cudaError_t e = launch_pdl(paged_decode_kernel, grid, dim3(kDecThreads), kDecSmemBytes, s, tmk,
-                             tmv, p);
+  // At most one CTA per SM: two page groups per CTA (see paged_decode_kernel).
+  const bool two = max_splits * num_kv_heads * batch <= (int64_t)sm_count();
+  cudaError_t e =
+      two ? launch_pdl(paged_decode_kernel<2>, grid, dim3(dec_threads(2)), dec_smem_bytes(2), s,
+                       tmk, tmv, p)
+          : launch_pdl(paged_decode_kernel<1>, grid, dim3(dec_threads(1)), dec_smem_bytes(1), s,
+                       tmk, tmv, p);
   if (e != cudaSuccess) return cuda_fail(e, "fi_paged_decode: launch");
   if (max_splits > 1) {
     dim3 g2((unsigned)((num_q_heads + 3) / 4), (unsigned)batch);

@@ -47,10 +47,13 @@ struct PeerGatherArgs {
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
   uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 
 __global__ void __launch_bounds__(kPgThreads) peer_gather_kernel(const PeerGatherArgs a) {
@@ -64,29 +67,33 @@ __global__ void __launch_bounds__(kPgThreads) peer_gather_kernel(const PeerGathe
     const int64_t off = a.data_off + r * a.row_total + a.rank * a.row_bytes + c * 16;
     for (int p = 0; p < a.world; ++p) *reinterpret_cast<uint4*>(a.base[p] + off) = v;
   }
-  __threadfence_system();
+  // One system-scope fence per CTA: the barrier orders the CTA's stores before it.
   __syncthreads();
   if (threadIdx.x != 0) return;
-  if (atomicAdd(a.counter, 1u) != gridDim.x - 1) return;
-  // Last CTA: every CTA's stores are fenced. Publish this call, then wait for the
-  // same call of every peer.
-  atomicExch(a.counter, 0u);
+  __threadfence_system();
+  if (gridDim.x > 1) {
+    if (atomicAdd(a.counter, 1u) != gridDim.x - 1) return;
+    // Last CTA: every CTA's stores were fenced before its arrival.
+    atomicExch(a.counter, 0u);
+    __threadfence_system();
+  }
+  // Publish this call to every rank, then wait for the same call of every rank.
   const uint32_t e = *a.epoch + 1;
   *a.epoch = e;
-  __threadfence_system();
   for (int p = 0; p < a.world; ++p)
     st_release_sys(reinterpret_cast<uint32_t*>(a.base[p] + a.flags_off) + a.rank, e);
   const uint32_t* mine = reinterpret_cast<const uint32_t*>(a.base[a.rank] + a.flags_off);
   const unsigned long long t0 = globaltimer_ns();
   for (int p = 0; p < a.world; ++p) {
     uint32_t spins = 0;
-    while ((int32_t)(ld_acquire_sys(mine + p) - e) < 0) {
+    while ((int32_t)(ld_relaxed_sys(mine + p) - e) < 0) {
       if ((++spins & 63u) == 0u && globaltimer_ns() - t0 > kWaitTimeoutNs) {
         set_error(a.err, FI_DEVERR_TIMEOUT);
         return;
       }
     }
   }
+  fence_acq_rel_sys();  // the peers' rows are visible to this kernel's successors
 }
 
 static int64_t pg_data_bytes(int64_t nbuf, int64_t max_rows, int64_t row_total) {
@@ -187,7 +194,7 @@ extern "C" int fi_peer_gather(const void* src, int64_t rows, int64_t row_bytes,
   a.counter = local + 1;
   a.err = error_flag;
   const int64_t total = rows * (row_bytes / 16);
-  int64_t blocks = (total + kPgThreads - 1) / kPgThreads;
+  int64_t blocks = (total + kPgThreads * 8 - 1) / (kPgThreads * 8);  // ~8 vectors a thread
   if (blocks < 1) blocks = 1;
   const int64_t cap = (int64_t)sm_count() * 4;
   if (blocks > cap) blocks = cap;

@@ -93,6 +93,27 @@ def test_config3_shape_vs_fp32(cuda_device, device_checks):
     _ok(out, paged_attention_fp32(q, kc, vc, bt, lens))
 
 
+@pytest.mark.parametrize("batch,hq,hkv,lo,hi,pps", [(16, 24, 8, 1024, 1280, 32),
+                                                    (16, 12, 4, 1024, 1280, 0),
+                                                    (16, 12, 4, 1024, 1280, 5),
+                                                    (3, 24, 8, 1, 2048, 32),
+                                                    (2, 6, 2, 4000, 4096, 0)])
+def test_small_grids_two_page_groups(cuda_device, device_checks, batch, hq, hkv, lo, hi, pps):
+    """Grids of at most one CTA per SM run two page groups per CTA, each with its own
+    ring: long unsplit sequences (up to 64 pages a CTA), repeated back to back."""
+    from fast_infer_b200.kernels.attention import paged_attention
+    rng = np.random.default_rng(batch * 1000 + hkv * 10 + pps)
+    lens = rng.integers(lo, hi + 1, size=batch).astype(np.int32)
+    q, kc, vc, bt = _random_paged(rng, lens, hq, hkv)
+    args = (_to(q, cuda_device), _to(kc, cuda_device), _to(vc, cuda_device),
+            _to(bt, cuda_device), 64, 0)
+    outs = [paged_attention(*args, context_lens=_to(lens, cuda_device), pages_per_split=pps,
+                            max_context_len=int(lens.max())) for _ in range(5)]
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    _ok(outs[0].cpu().numpy(), paged_attention_fp32(q, kc, vc, bt, lens))
+
+
 @pytest.mark.parametrize("hq,hkv", [(8, 8), (32, 4), (24, 8), (4, 2)])
 def test_gqa_group_sizes(cuda_device, device_checks, hq, hkv):
     from fast_infer_b200.kernels.attention import paged_attention
