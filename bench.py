@@ -429,7 +429,21 @@ def run_only(args):
     peaks, peak_kind = load_peaks()
     out = {"only": args.only, "steps": args.steps, "warmup": args.warmup}
     if args.only == "stack":
-        out.update(run_stack(torch, dev, 0, 1, None))
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        if world == 1:
+            out.update(run_stack(torch, dev, 0, 1, None))
+        else:  # under torchrun: one rank per GPU, rank 0 prints
+            import datetime
+            import torch.distributed as dist
+            rank, local = int(os.environ["RANK"]), int(os.environ["LOCAL_RANK"])
+            dev = torch.device("cuda", local)
+            torch.cuda.set_device(dev)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+            out.update(run_stack(torch, dev, rank, world, dist))
+            dist.barrier()
+            dist.destroy_process_group()
+            if rank != 0:
+                return
     elif args.only == "int4":
         out.update(run_int4(torch, dev, args.steps, args.warmup, float(peaks["hbm_gbs"]),
                             cpu=False))
