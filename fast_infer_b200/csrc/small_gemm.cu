@@ -1,0 +1,333 @@
+// Decode-sized fp16 GEMM with an optional RMSNorm prologue and residual epilogue:
+//   c[m, :] = (residual[m, :] +) norm(x[m, :]) @ w^T,   m < M <= 16,
+// w [N, K] fp16 (the reference's linear-weight layout, kernels/matmul.py:187-212
+// `_fp16_matmul`), fp32 accumulation, fp16 out (one rounding, after the residual).
+// norm(x) = the reference's RMSNorm (kernels/rms_norm.py:29-43) with the same fp32
+// arithmetic and reduction order as fi_rms_norm, so the normalised rows are the
+// ones fi_rms_norm would produce; without a norm weight x is used as is.
+//
+// Replaces, in the decode step of the attention stack (model.py:82-93,134-141 at
+// batch <= 16), the RMSNorm launch plus the QKV library GEMM, and the O-projection
+// GEMM plus the residual add. At these sizes the library GEMM streams the weights at
+// about half the HBM rate; the weights are the whole cost (M x K of x is ~100 KB).
+//
+// B200 design (same skeleton as the INT4 kernel): persistent CTAs, one TMA producer
+// warp streaming 16-row x 512-k weight tiles (one 3-D box of 8 x 128-byte chunks,
+// 128B-swizzled) into a ring; 8 math warps each take one 64-k chunk of every tile:
+// A fragments straight from the swizzled tile with ldmatrix, B = x^T fragments with
+// ldmatrix from x staged once per CTA in shared memory, mma.sync m16n8k16 computing
+// C^T = W x^T (weight rows = MMA M, tokens = N). The 8 warps' partial sums are added
+// in warp order through shared memory (deterministic). Every mbarrier wait is
+// bounded (FI_DEVERR_TIMEOUT). Launched with programmatic dependent launch: the
+// first ring of weight tiles goes to L2 before the wait for the previous kernel.
+#include <cuda_fp16.h>
+
+#include <cstring>
+
+#include "common.cuh"
+#include "host_common.h"
+
+namespace fi {
+
+constexpr int kSgWarps = 8;                        // math warps
+constexpr int kSgThreads = (kSgWarps + 1) * 32;    // + one TMA producer warp
+constexpr int kSgRows = 16;                        // weight rows (outputs) per work item
+constexpr int kSgChunk = 64;                       // k per math warp per round (128 bytes)
+constexpr int kSgRoundK = kSgWarps * kSgChunk;     // 512
+constexpr int kSgChunkBytes = kSgRows * 128;       // 2 KB: 16 rows x 64 fp16
+constexpr int kSgStageBytes = kSgWarps * kSgChunkBytes;  // 16 KB
+constexpr int kSgStages = 4;
+constexpr int kSgMaxM = 16;
+constexpr int kSgBar = 1;                          // named barrier of the math warps
+
+struct SgArgs {
+  const __half* x;
+  const __half* res;   // residual (nullable)
+  const __half* normw; // RMSNorm weight [K] (nullable)
+  __half* c;
+  int* err;
+  int M, N, K, rounds, xstride;
+  float eps;
+  int64_t xs0, cs0, cs1, rs0, rs1;
+};
+
+struct SgBars {
+  uint64_t full[kSgStages], empty[kSgStages];
+};
+
+template <int NT>
+__host__ __device__ constexpr size_t sg_red_bytes() {
+  return (size_t)kSgWarps * NT * 8 * (kSgRows + 1) * 4;
+}
+__host__ __device__ constexpr size_t sg_fixed_bytes() {
+  return 1024 + (size_t)kSgStages * kSgStageBytes + 256;
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kSgThreads, 1)
+    small_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const SgArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_align1024(smem_raw);
+  uint8_t* stages = smem;
+  SgBars* bars = reinterpret_cast<SgBars*>(stages + kSgStages * kSgStageBytes);
+  auto red = reinterpret_cast<float(*)[NT * 8][kSgRows + 1]>(reinterpret_cast<uint8_t*>(bars) + 256);
+  __half* xs = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(bars) + 256 + sg_red_bytes<NT>());
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int items = (a.N + kSgRows - 1) / kSgRows;
+  const int my_items = blockIdx.x < items ? (items - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  const int total = my_items * a.rounds;
+
+  if (tid == 0) {
+    for (int i = 0; i < kSgStages; ++i) {
+      mbar_init(&bars->full[i], 1);
+      mbar_init(&bars->empty[i], kSgWarps * 32);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  grid_dep_launch();
+
+  if (warp == kSgWarps) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tm_w);
+      for (int q = 0; q < total && q < kSgStages; ++q)  // weights only to L2 before the wait
+        tma_prefetch_l2_3d(&tm_w, 0, (blockIdx.x + (q / a.rounds) * gridDim.x) * kSgRows,
+                           (q % a.rounds) * kSgWarps);
+      grid_dep_wait();
+      bool dead = false;
+      for (int q = 0; q < total; ++q) {
+        const int st = q % kSgStages;
+        if (q >= kSgStages && !dead)
+          dead = !mbar_wait(&bars->empty[st], ((q / kSgStages) - 1) & 1, a.err);
+        const int item = blockIdx.x + (q / a.rounds) * gridDim.x, r = q % a.rounds;
+        mbar_arrive_expect_tx(&bars->full[st], kSgStageBytes);
+        // (element, row, 64-element chunk): 8 chunks x 16 rows x 128 bytes
+        tma_load_3d(stages + st * kSgStageBytes, &tm_w, &bars->full[st], 0, item * kSgRows,
+                    r * kSgWarps);
+      }
+      for (int q = total > kSgStages ? total - kSgStages : 0; q < total; ++q)
+        mbar_wait(&bars->full[q % kSgStages], (q / kSgStages) & 1, a.err);
+    }
+    return;
+  }
+
+  // ---------------------------------------------------------------- math warps
+  grid_dep_wait();  // x, the residual and the norm weight may be the previous kernel's output
+  {
+    // x -> shared memory [M][xstride], zero past K (up to the last round's end), with
+    // 8 independent 16-byte loads in flight per thread.
+    const int chunks = a.rounds * (kSgRoundK / 8), kchunks = a.K / 8;
+    const int total_c = a.M * chunks;
+    for (int i0 = tid; i0 < total_c; i0 += 8 * kSgWarps * 32) {
+      uint4 u[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = i0 + j * kSgWarps * 32;
+        const int m = i / chunks, c = i - m * chunks;
+        u[j] = make_uint4(0u, 0u, 0u, 0u);
+        if (i < total_c && c < kchunks)
+          u[j] = *reinterpret_cast<const uint4*>(a.x + m * a.xs0 + c * 8);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = i0 + j * kSgWarps * 32;
+        if (i >= total_c) break;
+        const int m = i / chunks, c = i - m * chunks;
+        *reinterpret_cast<uint4*>(xs + m * a.xstride + c * 8) = u[j];
+      }
+    }
+    named_bar_sync(kSgBar, kSgWarps * 32);
+    if (a.normw) {
+      // RMSNorm in place, one warp per token row, in fi_rms_norm's order: lane l sums
+      // x^2 over its 8-element vectors l, l+32, ... with fmaf, then a butterfly
+      // shuffle; out = (x * rsqrt(mean + eps)) * w rounded to fp16.
+      const int vecs = a.K / 8;
+      for (int m = warp; m < a.M; m += kSgWarps) {
+        __half* row = xs + m * a.xstride;
+        float ss = 0.f;
+        for (int v = lane; v < vecs; v += 32) {
+          const uint4 u = *reinterpret_cast<const uint4*>(row + v * 8);
+          const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(h[e]);
+            ss = fmaf(f.x, f.x, ss);
+            ss = fmaf(f.y, f.y, ss);
+          }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        const float rms = rsqrtf(ss / (float)a.K + a.eps);
+        for (int v = lane; v < vecs; v += 32) {
+          uint4 u = *reinterpret_cast<const uint4*>(row + v * 8);
+          const uint4 wu = __ldg(reinterpret_cast<const uint4*>(a.normw + v * 8));
+          __half2* h = reinterpret_cast<__half2*>(&u);
+          const __half2* wh = reinterpret_cast<const __half2*>(&wu);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(h[e]);
+            const float2 g = __half22float2(wh[e]);
+            h[e] = __floats2half2_rn(f.x * rms * g.x, f.y * rms * g.y);
+          }
+          *reinterpret_cast<uint4*>(row + v * 8) = u;
+        }
+      }
+      named_bar_sync(kSgBar, kSgWarps * 32);
+    }
+  }
+
+  const int g = lane >> 2, t = lane & 3;
+  // ldmatrix row addresses. A: weight rows lane & 15, k half lane >> 4 of each k16
+  // step. B: token (lane & 7) of tile nt (tokens past M read row M-1: computed, never
+  // stored), k = 8 * (lane >> 3) within a 32-k pair of steps.
+  uint32_t xrow[NT];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+    xrow[nt] = smem_u32(xs + min(nt * 8 + (lane & 7), a.M - 1) * a.xstride + (lane >> 3) * 8);
+  const int arow = lane & 15, ahalf = lane >> 4;
+
+  float acc[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+
+  bool dead = false;
+  int q = 0;
+  for (int j = 0; j < my_items; ++j) {
+    const int item = blockIdx.x + j * gridDim.x;
+    for (int r = 0; r < a.rounds; ++r, ++q) {
+      const int st = q % kSgStages;
+      if (!dead) dead = !__all_sync(0xffffffffu, mbar_wait(&bars->full[st], (q / kSgStages) & 1, a.err));
+      const uint32_t region = smem_u32(stages + st * kSgStageBytes + warp * kSgChunkBytes);
+      uint32_t af[4][4];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        ldsm_x4(region + arow * 128 + (((kk * 2 + ahalf) ^ (arow & 7)) << 4), af[kk][0],
+                af[kk][1], af[kk][2], af[kk][3]);
+      // The stage is released once its values are in registers; the next write to
+      // it is a TMA (async proxy) write, so order these reads before it.
+      fence_proxy_async_smem();
+      mbar_arrive(&bars->empty[st]);
+      const uint32_t kbyte = (uint32_t)(r * kSgRoundK + warp * kSgChunk) * 2;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int kp = 0; kp < 2; ++kp) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(xrow[nt] + kbyte + kp * 64, b0, b1, b2, b3);
+          mma_16816(acc[nt], af[2 * kp][0], af[2 * kp][1], af[2 * kp][2], af[2 * kp][3], b0, b1);
+          mma_16816(acc[nt], af[2 * kp + 1][0], af[2 * kp + 1][1], af[2 * kp + 1][2],
+                    af[2 * kp + 1][3], b2, b3);
+        }
+      }
+    }
+    // ---- item done: add the 8 warps' partial sums in warp order, residual, store
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        // C^T fragment: weight row g + 8*(e>>1), token nt*8 + 2t + (e&1)
+        red[warp][nt * 8 + 2 * t + (e & 1)][g + (e >> 1) * 8] = acc[nt][e];
+        acc[nt][e] = 0.f;
+      }
+    named_bar_sync(kSgBar, kSgWarps * 32);
+    const int nbase = item * kSgRows;
+    for (int i = tid; i < a.M * kSgRows; i += kSgWarps * 32) {
+      const int m = i / kSgRows, rr = i - m * kSgRows, n = nbase + rr;
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < kSgWarps; ++w) sum += red[w][m][rr];
+      if (n < a.N) {
+        if (a.res) sum += __half2float(a.res[m * a.rs0 + n * a.rs1]);
+        a.c[m * a.cs0 + n * a.cs1] = __float2half_rn(sum);
+      }
+    }
+    named_bar_sync(kSgBar, kSgWarps * 32);
+  }
+}
+
+template <int NT>
+static int launch_small_gemm(cudaStream_t st, const CUtensorMap& tm, const SgArgs& a,
+                             size_t smem) {
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(small_gemm_kernel<NT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+    if (e != cudaSuccess) return cuda_fail(e, "fi_small_gemm: cudaFuncSetAttribute");
+    attr_done[dev] = true;
+  }
+  const int items = (a.N + kSgRows - 1) / kSgRows;
+  int grid = sm_count();
+  if (grid > items) grid = items;
+  cudaError_t e = launch_pdl(small_gemm_kernel<NT>, dim3((unsigned)grid), dim3(kSgThreads), smem,
+                             st, tm, a);
+  if (e != cudaSuccess) return cuda_fail(e, "fi_small_gemm launch");
+  return FI_OK;
+}
+
+}  // namespace fi
+
+extern "C" int fi_small_gemm(const void* x, const void* w, void* c, const void* residual,
+                             const void* norm_weight, float eps, int64_t m, int64_t n, int64_t k,
+                             const int64_t* x_strides, const int64_t* w_strides,
+                             const int64_t* c_strides, const int64_t* residual_strides,
+                             int32_t* error_flag, void* stream) {
+  using namespace fi;
+  clear_error();
+  if (m < 0 || n < 0 || k <= 0) return fail(FI_ERR_INVALID_ARG, "fi_small_gemm: bad sizes");
+  if (m > kSgMaxM)
+    return fail(FI_ERR_UNSUPPORTED, "fi_small_gemm: M (%lld) > %d; use a dense GEMM",
+                (long long)m, kSgMaxM);
+  if (k % kSgChunk != 0 || k > (1 << 20) || n > (1 << 30))
+    return fail(FI_ERR_UNSUPPORTED, "fi_small_gemm: K must be a multiple of 64 (and <= 2^20)");
+  if (m == 0 || n == 0) return FI_OK;
+  if (!x || !w || !c || !x_strides || !w_strides || !c_strides || (residual && !residual_strides))
+    return fail(FI_ERR_INVALID_ARG, "fi_small_gemm: null pointer argument");
+  if (x_strides[1] != 1 || x_strides[0] % 8 != 0 || !aligned16(x) || w_strides[1] != 1 ||
+      w_strides[0] % 8 != 0 || !aligned16(w) || (norm_weight && !aligned16(norm_weight)))
+    return fail(FI_ERR_ALIGNMENT,
+                "fi_small_gemm: x / w need 16-byte aligned bases, unit inner strides and row "
+                "strides that are multiples of 8 elements");
+  CUtensorMap tm;
+  {
+    const uint64_t dims[3] = {(uint64_t)kSgChunk, (uint64_t)n, (uint64_t)(k / kSgChunk)};
+    const uint64_t sb[2] = {(uint64_t)w_strides[0] * 2, 128};
+    const uint32_t box[3] = {(uint32_t)kSgChunk, (uint32_t)kSgRows, (uint32_t)kSgWarps};
+    const int r = encode_tiled(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, w, dims, sb, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B, "fi_small_gemm w");
+    if (r != FI_OK) return r;
+  }
+  SgArgs a;
+  memset(&a, 0, sizeof(a));
+  a.x = static_cast<const __half*>(x);
+  a.res = static_cast<const __half*>(residual);
+  a.normw = static_cast<const __half*>(norm_weight);
+  a.c = static_cast<__half*>(c);
+  a.err = error_flag;
+  a.M = (int)m;
+  a.N = (int)n;
+  a.K = (int)k;
+  a.rounds = (int)((k + kSgRoundK - 1) / kSgRoundK);
+  a.xstride = a.rounds * kSgRoundK + 8;  // + 16 bytes: conflict-free ldmatrix rows
+  a.eps = eps;
+  a.xs0 = x_strides[0];
+  a.cs0 = c_strides[0];
+  a.cs1 = c_strides[1];
+  if (residual) {
+    a.rs0 = residual_strides[0];
+    a.rs1 = residual_strides[1];
+  }
+  const int nt = m <= 8 ? 1 : 2;
+  const size_t smem = sg_fixed_bytes() + (nt == 1 ? sg_red_bytes<1>() : sg_red_bytes<2>()) +
+                      (size_t)m * a.xstride * 2;
+  if (smem > 232448)
+    return fail(FI_ERR_UNSUPPORTED, "fi_small_gemm: K too large to stage x in shared memory");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return nt == 1 ? launch_small_gemm<1>(st, tm, a, smem) : launch_small_gemm<2>(st, tm, a, smem);
+}

@@ -163,3 +163,70 @@ def fuse_qkv_inplace(weights: dict):
             sa["qkv_proj"] = cat([sa.pop("q_proj"), sa.pop("k_proj"), sa.pop("v_proj")])
         if "gate_up_proj" not in mlp:
             mlp["gate_up_proj"] = cat([mlp.pop("gate_proj"), mlp.pop("up_proj")])
+
+
+# fi_small_gemm handles up to 16 rows; measured against the library GEMM (+ a separate
+# RMSNorm) on the Llama-3.2-3B attention projections it is faster up to 8 rows
+# (o projection at 1 row: 6.8 vs 11.7 us) and slower at 16 (QKV: 11.4 vs 9.2 us), so
+# larger batches take the library path.
+SMALL_GEMM_MAX_M = 8
+
+
+def fp16_linear(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor = None,
+                norm_weight: torch.Tensor = None, eps: float = 1e-5,
+                out: torch.Tensor = None) -> torch.Tensor:
+    """``residual + rms_norm(x, norm_weight, eps) @ w.T`` in fp16 (fp32 accumulation).
+
+    x [..., K], w [N, K] fp16 (the reference's linear layout, kernels/matmul.py:187-212);
+    residual [..., N] or None; norm_weight [K] or None (no norm). Up to 16 rows of x
+    take one ``fi_small_gemm`` launch (norm on load, residual in the epilogue, a single
+    rounding) up to ``SMALL_GEMM_MAX_M`` rows; more rows use ``rms_norm`` and the dense
+    library GEMM with the residual as its beta = 1 input. ``out`` (may be
+    ``residual``) receives the result.
+    """
+    if not x.is_cuda or not w.is_cuda:
+        raise ValueError("x and w must be CUDA tensors (fast_infer_b200 has no CPU path)")
+    if x.dtype != torch.float16 or w.dtype != torch.float16:
+        raise TypeError("fp16_linear expects float16 x and w")
+    K = x.shape[-1]
+    if w.dim() != 2 or w.shape[1] != K:
+        raise ValueError(f"w must be [N, {K}]")
+    N = w.shape[0]
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, K)
+    M = x2.shape[0]
+    r2 = residual.reshape(-1, N) if residual is not None else None
+    if r2 is not None and r2.shape[0] != M:
+        raise ValueError("residual must be [..., N] with x's leading shape")
+    if out is None:
+        out = torch.empty(*lead, N, dtype=torch.float16, device=x.device)
+    o2 = out.view(-1, N)
+    if M <= SMALL_GEMM_MAX_M and K % 64 == 0 and M > 0 and N > 0:
+        if x2.stride(1) != 1 or x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
+            x2 = x2.contiguous()
+        if w.stride(1) != 1 or w.stride(0) % 8 != 0 or w.data_ptr() % 16 != 0:
+            w = w.contiguous()
+        nw = norm_weight
+        if nw is not None and (not nw.is_contiguous() or nw.data_ptr() % 16 != 0):
+            nw = nw.contiguous()
+        lib = _lib.load()
+        with with_device(x.device):
+            err = error_word(x.device)
+            st = lib.fi_small_gemm(
+                x2.data_ptr(), w.data_ptr(), o2.data_ptr(),
+                r2.data_ptr() if r2 is not None else None,
+                nw.data_ptr() if nw is not None else None, float(eps), M, N, K,
+                _lib.strides(*x2.stride()), _lib.strides(*w.stride()),
+                _lib.strides(*o2.stride()),
+                _lib.strides(*r2.stride()) if r2 is not None else None,
+                err.data_ptr() if err is not None else None, stream_of(x.device))
+            _lib.check(st, "fp16_linear")
+            device_errors(err, "fp16_linear")
+        return out
+    from fast_infer_b200.kernels.rms_norm import rms_norm
+    h = rms_norm(x2, norm_weight, eps) if norm_weight is not None else x2
+    if r2 is not None:
+        torch.addmm(r2, h, w.t(), out=o2) if o2.data_ptr() != r2.data_ptr() else o2.addmm_(h, w.t())
+    else:
+        torch.matmul(h, w.t(), out=o2)
+    return out

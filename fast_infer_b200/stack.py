@@ -36,6 +36,7 @@ import torch
 
 from fast_infer_b200._runtime import device_checks
 from fast_infer_b200.kernels.attention import flash_attention, paged_attention
+from fast_infer_b200.kernels.matmul import fp16_linear
 from fast_infer_b200.kernels.rms_norm import rms_norm
 from fast_infer_b200.kv_cache import KVCache, rope_and_store
 from fast_infer_b200.shard import HeadShard, PeerGather, gather_heads, head_shard
@@ -100,8 +101,10 @@ class AttentionStack:
             q_cols = slice(sh.q_start * head_dim, sh.q_end * head_dim)
             kv_cols = slice(sh.kv_start * head_dim, sh.kv_end * head_dim)
             wqkv = torch.cat([wq[:, q_cols], wk[:, kv_cols], wv[:, kv_cols]], dim=1)
-            self.layers.append(dict(norm=norm.half(), wqkv=wqkv.half().contiguous(),
-                                    wo=wo.half().contiguous()))
+            # weights kept as [out, in] (the reference's linear layout): the decode GEMMs
+            # stream them row by row, the prefill GEMMs read them transposed
+            self.layers.append(dict(norm=norm.half(), wqkv_t=wqkv.t().half().contiguous(),
+                                    wo_t=wo.t().half().contiguous()))
         self.cos, self.sin = precompute_freqs(head_dim, max_seq_len, rope_theta, self.device)
         pages_per_seq = (max_seq_len + 63) // 64
         self.cache = KVCache(num_layers, sh.num_kv_heads, head_dim, max_seq_len, 64, self.device,
@@ -122,13 +125,13 @@ class AttentionStack:
         return self.gather(o)
 
     @staticmethod
-    def _residual(h: torch.Tensor, o: torch.Tensor, wo: torch.Tensor) -> None:
-        """h += o @ wo as one GEMM with beta = 1 (h contiguous, updated in place)."""
-        h.view(-1, h.shape[-1]).addmm_(o.reshape(-1, o.shape[-1]), wo)
+    def _residual(h: torch.Tensor, o: torch.Tensor, wo_t: torch.Tensor) -> None:
+        """h += o @ wo_t.T as one GEMM with beta = 1 (h contiguous, updated in place)."""
+        h.view(-1, h.shape[-1]).addmm_(o.reshape(-1, o.shape[-1]), wo_t.t())
 
     # ------------------------------------------------------------------ prefill
     def _qkv(self, w, h):
-        return rms_norm(h, w["norm"], self.eps) @ w["wqkv"]
+        return rms_norm(h, w["norm"], self.eps) @ w["wqkv_t"].t()
 
     def prefill(self, h: torch.Tensor) -> torch.Tensor:
         """Prompt pass (reference model.py:67-69, 101-117): h [B, S, hidden] fp16.
@@ -149,7 +152,7 @@ class AttentionStack:
             v = qkv[..., (nq + nkv) * D:].view(B, S, nkv, D)
             o = flash_attention(q_rot.transpose(1, 2), k_rot.transpose(1, 2), v.transpose(1, 2))
             o = self._gather(o.transpose(1, 2).reshape(B, S, nq * D))
-            self._residual(h, o, w["wo"])
+            self._residual(h, o, w["wo_t"])
         self.token_count = S
         return h
 
@@ -181,13 +184,14 @@ class AttentionStack:
         span = self.cache.max_blocks_per_seq * 64
         h = self._h_in.clone()  # the residual stream is updated in place below
         for li, w in enumerate(self.layers):
-            q = rope_and_store(self.cache, li, self._qkv(w, h), nq, self.cos, self.sin,
-                               self._dev_start)
+            # RMSNorm + QKV projection in one launch at decode batch sizes
+            qkv = fp16_linear(h, w["wqkv_t"], norm_weight=w["norm"], eps=self.eps)
+            q = rope_and_store(self.cache, li, qkv, nq, self.cos, self.sin, self._dev_start)
             o = paged_attention(q[:, 0], self.cache.k[li], self.cache.v[li],
                                 self.cache.block_table, 64, 0, context_lens=self._dev_ctx,
                                 max_context_len=span, workspace=self._ws)
             o = self._gather(o.reshape(B, 1, nq * D), li)
-            self._residual(h, o, w["wo"])
+            fp16_linear(o, w["wo_t"], residual=h, out=h)  # h += o @ Wo, one launch
         self._dev_ctx.add_(1)
         self._dev_start.add_(1)
         self._h_in.copy_(h)

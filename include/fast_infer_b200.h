@@ -276,6 +276,25 @@ int fi_int4_quantize(const void* w, void* packed, void* scales, int64_t n, int64
                      const int64_t* scales_strides, void* stream);
 
 /*
+ * Decode-sized fp16 GEMM with optional RMSNorm prologue and residual epilogue:
+ *   c[i, :] = residual[i, :] + rmsnorm(x[i, :]) @ w^T   (i < m <= 16)
+ * x [m, k], w [n, k] (the reference's linear-weight layout), c / residual [m, n], all
+ * fp16 (strides: 2 entries; x and w with unit inner stride, row strides multiples of
+ * 8 elements, 16-byte aligned bases); fp32 accumulation, one fp16 rounding at the
+ * end. norm_weight [k] (NULL: no norm) applies fi_rms_norm's arithmetic with eps;
+ * residual NULL: no add (it may alias c). k a multiple of 64; m > 16 returns
+ * FI_ERR_UNSUPPORTED (use a dense GEMM).
+ *
+ * Replaces, at decode batch sizes: kernels/rms_norm.py:29-43 followed by
+ * kernels/matmul.py:187-212 `_fp16_matmul` (the QKV projection of model.py:82-93),
+ * and `_fp16_matmul` followed by the residual add (the O projection, model.py:134-141).
+ */
+int fi_small_gemm(const void* x, const void* w, void* c, const void* residual,
+                  const void* norm_weight, float eps, int64_t m, int64_t n, int64_t k,
+                  const int64_t* x_strides, const int64_t* w_strides, const int64_t* c_strides,
+                  const int64_t* residual_strides, int32_t* error_flag, void* stream);
+
+/*
  * Head-output all-gather over NVLink peer memory, for a stack sharded by KV head.
  *
  * Replaces: the NCCL all-gather of per-rank attention outputs [rows, heads_r * 128]

@@ -132,3 +132,18 @@ def test_int4_validation():
                                _lib.strides(250, 1), None) == _lib.FI_ERR_ALIGNMENT
     assert lib.fi_int4_quantize(1, 1, 1, 8, 256, 127, s2, s2, s2, None) == _lib.FI_ERR_INVALID_ARG
     assert lib.fi_int4_quantize(1, 1, 1, 0, 256, 128, s2, s2, s2, None) == _lib.FI_OK
+
+
+def test_small_gemm_validation():
+    from fast_infer_b200 import _lib
+    lib = _lib.load()
+    s2 = _lib.strides(1, 1)
+    # more than 16 rows, K not a multiple of 64, null pointers: rejected on the host
+    assert lib.fi_small_gemm(None, None, None, None, None, 1e-5, 17, 8, 64, s2, s2, s2, None,
+                             None, None) == _lib.FI_ERR_UNSUPPORTED
+    assert lib.fi_small_gemm(None, None, None, None, None, 1e-5, 4, 8, 100, s2, s2, s2, None,
+                             None, None) == _lib.FI_ERR_UNSUPPORTED
+    assert lib.fi_small_gemm(None, None, None, None, None, 1e-5, 4, 8, 64, s2, s2, s2, None,
+                             None, None) == _lib.FI_ERR_INVALID_ARG
+    assert lib.fi_small_gemm(None, None, None, None, None, 1e-5, 0, 8, 64, s2, s2, s2, None,
+                             None, None) == _lib.FI_OK

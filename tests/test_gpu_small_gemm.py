@@ -1,0 +1,80 @@
+"""Decode-sized fp16 GEMM (fi_small_gemm via kernels.matmul.fp16_linear): against an
+fp32 reference within one fp16 ulp of the output plus 1e-3 (rel-L2 <= 1e-3); the
+fused RMSNorm prologue gives the same bits as fi_rms_norm followed by the plain GEMM;
+residual in place; ragged N and K; deterministic; more than 16 rows fall back to the
+dense library path with the same semantics."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _kernel_up_to_16_rows(monkeypatch):
+    """Route every size the kernel supports (up to 16 rows) through fi_small_gemm."""
+    import fast_infer_b200.kernels.matmul as mm
+    monkeypatch.setattr(mm, "SMALL_GEMM_MAX_M", 16)
+
+
+def _close(out, ref):
+    out, ref = out.float(), ref.float()
+    err = (out - ref).abs()
+    ok = bool((err <= 1e-3 + ref.abs() * 2.0 ** -10).all())
+    rel = float((out - ref).norm() / ref.norm().clamp_min(1e-30))
+    return ok and rel <= 1e-3, float(err.max()), rel
+
+
+def _data(m, n, k, dev, seed):
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    x = torch.randn(m, k, device=dev, generator=g).half()
+    w = (torch.randn(n, k, device=dev, generator=g) * 0.02).half()
+    res = torch.randn(m, n, device=dev, generator=g).half()
+    nw = (1 + 0.1 * torch.randn(k, device=dev, generator=g)).half()
+    return x, w, res, nw
+
+
+@pytest.mark.parametrize("m", [1, 5, 8, 9, 16])
+@pytest.mark.parametrize("n,k", [(2560, 3072), (3072, 3072), (100, 192), (17, 64), (5120, 3072)])
+def test_against_fp32(cuda_device, m, n, k):
+    from fast_infer_b200.kernels.matmul import fp16_linear
+    from fast_infer_b200.kernels.rms_norm import rms_norm
+    x, w, res, nw = _data(m, n, k, cuda_device, m * 131 + n + k)
+    plain = fp16_linear(x, w)
+    ok = _close(plain, x.float() @ w.float().t())
+    assert ok[0], ("plain", ok)
+    xn = rms_norm(x, nw, 1e-5)
+    full = fp16_linear(x, w, residual=res, norm_weight=nw)
+    ok = _close(full, res.float() + xn.float() @ w.float().t())
+    assert ok[0], ("norm+residual", ok)
+    # the fused norm reproduces fi_rms_norm bit for bit
+    assert torch.equal(fp16_linear(x, w, norm_weight=nw), fp16_linear(xn, w))
+
+
+def test_residual_in_place_and_determinism(cuda_device):
+    from fast_infer_b200.kernels.matmul import fp16_linear
+    x, w, res, nw = _data(16, 3072, 3072, cuda_device, 7)
+    expect = fp16_linear(x, w, residual=res, norm_weight=nw)
+    h = res.clone()
+    fp16_linear(x, w, residual=h, norm_weight=nw, out=h)
+    assert torch.equal(h, expect)
+    for _ in range(3):
+        assert torch.equal(fp16_linear(x, w, residual=res, norm_weight=nw), expect)
+
+
+def test_leading_dims_strides_and_fallback(cuda_device):
+    from fast_infer_b200.kernels.matmul import fp16_linear
+    from fast_infer_b200.kernels.rms_norm import rms_norm
+    x, w, res, nw = _data(12, 768, 1024, cuda_device, 9)
+    wide = torch.zeros(12, 1024 + 64, dtype=torch.float16, device=cuda_device)
+    wide[:, 32:32 + 1024] = x
+    a = fp16_linear(wide[:, 32:32 + 1024], w, residual=res, norm_weight=nw)
+    b = fp16_linear(x.reshape(3, 4, 1024), w, residual=res.reshape(3, 4, 768), norm_weight=nw)
+    assert b.shape == (3, 4, 768)
+    assert torch.equal(a, b.reshape(12, 768))
+    # 40 rows: the dense path, same semantics
+    x4, w4, r4, n4 = _data(40, 768, 1024, cuda_device, 10)
+    big = fp16_linear(x4, w4, residual=r4, norm_weight=n4)
+    ref = r4.float() + rms_norm(x4, n4).float() @ w4.float().t()
+    assert _close(big, ref)[0]

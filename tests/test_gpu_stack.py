@@ -26,7 +26,7 @@ def _fp32_attention_stack(stack, prompt, steps):
         cos, sin = stack.cos[pos].half(), stack.sin[pos].half()
         for li, w in enumerate(stack.layers):
             x = rms_norm(h, w["norm"], stack.eps)
-            q, k, v = (x @ w["wqkv"]).split([hq * D, hkv * D, hkv * D], dim=-1)
+            q, k, v = (x @ w["wqkv_t"].t()).split([hq * D, hkv * D, hkv * D], dim=-1)
             q = apply_rope(q.view(B, n, hq, D), cos, sin)
             k = apply_rope(k.view(B, n, hkv, D), cos, sin)
             v = v.view(B, n, hkv, D)
@@ -39,7 +39,7 @@ def _fp32_attention_stack(stack, prompt, steps):
             qpos = torch.arange(tot - n, tot, device=h.device)[:, None]
             s = s.masked_fill(torch.arange(tot, device=h.device)[None, :] > qpos, float("-inf"))
             o = (torch.softmax(s, -1) @ vv).transpose(1, 2).reshape(B, n, hq * D).half()
-            h = h + o @ w["wo"]
+            h = h + o @ w["wo_t"].t()
         return h
 
     h = run(prompt, 0)[:, -1:]
