@@ -271,6 +271,260 @@ static int launch_small_gemm(cudaStream_t st, const CUtensorMap& tm, const SgArg
   return FI_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Streamed variant: x arrives by TMA together with each weight tile (16 KB of
+// weights + 16 KB of x per round, 3-stage ring), so nothing is staged before the
+// first MMA and two CTAs share an SM. With kFold the weights come pre-multiplied by
+// the RMSNorm weight (w'[n, k] = fp16(w[n, k] * g[k])) and the per-token factor
+// rsqrt(mean(x^2) + eps) is taken from the x tiles of the CTA's first item and
+// applied in the epilogue: out = rms[m] * sum_k x[m, k] w'[n, k].
+constexpr int kSsStages = 3;
+constexpr int kSsStageBytes = 2 * kSgStageBytes;  // weights | x
+
+struct SsArgs {
+  const __half* res;
+  __half* c;
+  int* err;
+  int M, N, K, rounds;
+  float eps;
+  int64_t cs0, cs1, rs0, rs1;
+};
+
+template <int NT>
+__host__ __device__ constexpr size_t ss_smem_bytes() {
+  return 1024 + (size_t)kSsStages * kSsStageBytes + 256 + sg_red_bytes<NT>() +
+         (size_t)kSgWarps * 16 * 4 + 16 * 4;
+}
+
+template <int NT, bool kFold>
+__global__ void __launch_bounds__(kSgThreads, 2)
+    small_gemm_stream_kernel(const __grid_constant__ CUtensorMap tm_w,
+                             const __grid_constant__ CUtensorMap tm_x, const SsArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_align1024(smem_raw);
+  uint8_t* stages = smem;
+  SgBars* bars = reinterpret_cast<SgBars*>(stages + kSsStages * kSsStageBytes);
+  auto red = reinterpret_cast<float(*)[NT * 8][kSgRows + 1]>(reinterpret_cast<uint8_t*>(bars) + 256);
+  float* ssq = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256 + sg_red_bytes<NT>());
+  float* rmsv = ssq + kSgWarps * 16;  // [16]
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int items = (a.N + kSgRows - 1) / kSgRows;
+  const int my_items = blockIdx.x < items ? (items - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  const int total = my_items * a.rounds;
+
+  if (tid == 0) {
+    for (int i = 0; i < kSsStages; ++i) {
+      mbar_init(&bars->full[i], 1);
+      mbar_init(&bars->empty[i], kSgWarps * 32);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  grid_dep_launch();
+
+  if (warp == kSgWarps) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tm_w);
+      prefetch_tmap(&tm_x);
+      for (int q = 0; q < total && q < kSsStages; ++q)  // weights only to L2 before the wait
+        tma_prefetch_l2_3d(&tm_w, 0, (blockIdx.x + (q / a.rounds) * gridDim.x) * kSgRows,
+                           (q % a.rounds) * kSgWarps);
+      grid_dep_wait();  // x is the previous kernel's output
+      bool dead = false;
+      for (int q = 0; q < total; ++q) {
+        const int st = q % kSsStages;
+        if (q >= kSsStages && !dead)
+          dead = !mbar_wait(&bars->empty[st], ((q / kSsStages) - 1) & 1, a.err);
+        const int item = blockIdx.x + (q / a.rounds) * gridDim.x, r = q % a.rounds;
+        uint8_t* sp = stages + st * kSsStageBytes;
+        mbar_arrive_expect_tx(&bars->full[st], kSsStageBytes);
+        tma_load_3d(sp, &tm_w, &bars->full[st], 0, item * kSgRows, r * kSgWarps);
+        // x rows past M read as zeros (outside the tensor)
+        tma_load_3d(sp + kSgStageBytes, &tm_x, &bars->full[st], 0, 0, r * kSgWarps);
+      }
+      for (int q = total > kSsStages ? total - kSsStages : 0; q < total; ++q)
+        mbar_wait(&bars->full[q % kSsStages], (q / kSsStages) & 1, a.err);
+    }
+    return;
+  }
+
+  // ---------------------------------------------------------------- math warps
+  grid_dep_wait();  // the residual may be the previous kernel's output
+  const int g = lane >> 2, t = lane & 3;
+  const int arow = lane & 15, ahalf = lane >> 4;
+  float acc[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+  float ss[NT];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) ss[nt] = 0.f;
+
+  bool dead = false;
+  int q = 0;
+  for (int j = 0; j < my_items; ++j) {
+    const int item = blockIdx.x + j * gridDim.x;
+    for (int r = 0; r < a.rounds; ++r, ++q) {
+      const int st = q % kSsStages;
+      if (!dead) dead = !__all_sync(0xffffffffu, mbar_wait(&bars->full[st], (q / kSsStages) & 1, a.err));
+      const uint32_t wreg = smem_u32(stages + st * kSsStageBytes + warp * kSgChunkBytes);
+      const uint32_t xreg = wreg + kSgStageBytes;
+      uint32_t af[4][4], bf[NT][2][4];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        ldsm_x4(wreg + arow * 128 + (((kk * 2 + ahalf) ^ (arow & 7)) << 4), af[kk][0], af[kk][1],
+                af[kk][2], af[kk][3]);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int xr = nt * 8 + (lane & 7);  // token row of this lane's ldmatrix address
+#pragma unroll
+        for (int kp = 0; kp < 2; ++kp)
+          ldsm_x4(xreg + xr * 128 + (((kp * 4 + (lane >> 3)) ^ (xr & 7)) << 4), bf[nt][kp][0],
+                  bf[nt][kp][1], bf[nt][kp][2], bf[nt][kp][3]);
+      }
+      // Both tiles are in registers: release the stage (the next write to it is a
+      // TMA write, so order these reads before it).
+      fence_proxy_async_smem();
+      mbar_arrive(&bars->empty[st]);
+      if (kFold && j == 0) {
+        // this thread's x values of token nt*8 + g: 16 of the warp's 64 k per round
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int kp = 0; kp < 2; ++kp)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&bf[nt][kp][e]));
+              ss[nt] = fmaf(f.x, f.x, fmaf(f.y, f.y, ss[nt]));
+            }
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int kp = 0; kp < 2; ++kp) {
+          mma_16816(acc[nt], af[2 * kp][0], af[2 * kp][1], af[2 * kp][2], af[2 * kp][3],
+                    bf[nt][kp][0], bf[nt][kp][1]);
+          mma_16816(acc[nt], af[2 * kp + 1][0], af[2 * kp + 1][1], af[2 * kp + 1][2],
+                    af[2 * kp + 1][3], bf[nt][kp][2], bf[nt][kp][3]);
+        }
+    }
+    // ---- item done: warp partial sums in warp order (x the rms factor), residual
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        red[warp][nt * 8 + 2 * t + (e & 1)][g + (e >> 1) * 8] = acc[nt][e];
+        acc[nt][e] = 0.f;
+      }
+    if (kFold && j == 0) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        float v = ss[nt];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        if (t == 0) ssq[warp * 16 + nt * 8 + g] = v;
+      }
+      named_bar_sync(kSgBar, kSgWarps * 32);
+      if (tid < 16) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kSgWarps; ++w) v += ssq[w * 16 + tid];
+        rmsv[tid] = rsqrtf(v / (float)a.K + a.eps);
+      }
+    }
+    named_bar_sync(kSgBar, kSgWarps * 32);
+    const int nbase = item * kSgRows;
+    for (int i = tid; i < a.M * kSgRows; i += kSgWarps * 32) {
+      const int m = i / kSgRows, rr = i - m * kSgRows, n = nbase + rr;
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < kSgWarps; ++w) sum += red[w][m][rr];
+      if (kFold) sum *= rmsv[m];
+      if (n < a.N) {
+        if (a.res) sum += __half2float(a.res[m * a.rs0 + n * a.rs1]);
+        a.c[m * a.cs0 + n * a.cs1] = __float2half_rn(sum);
+      }
+    }
+    named_bar_sync(kSgBar, kSgWarps * 32);
+  }
+}
+
+template <int NT, bool kFold>
+static int launch_small_gemm_stream(cudaStream_t st, const CUtensorMap& tw, const CUtensorMap& tx,
+                                    const SsArgs& a) {
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  constexpr size_t smem = ss_smem_bytes<NT>();
+  if (!attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(small_gemm_stream_kernel<NT, kFold>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e, "fi_small_gemm: cudaFuncSetAttribute");
+    attr_done[dev] = true;
+  }
+  int nb = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, small_gemm_stream_kernel<NT, kFold>,
+                                                    kSgThreads, smem) != cudaSuccess || nb < 1)
+    nb = 1;
+  const int items = (a.N + kSgRows - 1) / kSgRows;
+  int grid = nb * sm_count();
+  if (grid > items) grid = items;
+  cudaError_t e = launch_pdl(small_gemm_stream_kernel<NT, kFold>, dim3((unsigned)grid),
+                             dim3(kSgThreads), smem, st, tw, tx, a);
+  if (e != cudaSuccess) return cuda_fail(e, "fi_small_gemm launch");
+  return FI_OK;
+}
+
+// Tensor maps and launch of the streamed variant (x [m, k] and w [n, k] already
+// checked by the caller).
+static int small_gemm_streamed(const void* x, const void* w, void* c, const void* residual,
+                               bool fold, float eps, int64_t m, int64_t n, int64_t k,
+                               const int64_t* x_strides, const int64_t* w_strides,
+                               const int64_t* c_strides, const int64_t* residual_strides,
+                               int32_t* error_flag, cudaStream_t st) {
+  CUtensorMap tw, tx;
+  const uint32_t box[3] = {(uint32_t)kSgChunk, (uint32_t)kSgRows, (uint32_t)kSgWarps};
+  {
+    const uint64_t dims[3] = {(uint64_t)kSgChunk, (uint64_t)n, (uint64_t)(k / kSgChunk)};
+    const uint64_t sb[2] = {(uint64_t)w_strides[0] * 2, 128};
+    const int r = encode_tiled(&tw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, w, dims, sb, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B, "fi_small_gemm w");
+    if (r != FI_OK) return r;
+  }
+  {
+    const uint64_t dims[3] = {(uint64_t)kSgChunk, (uint64_t)m, (uint64_t)(k / kSgChunk)};
+    const uint64_t sb[2] = {(uint64_t)x_strides[0] * 2, 128};
+    const int r = encode_tiled(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, x, dims, sb, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B, "fi_small_gemm x");
+    if (r != FI_OK) return r;
+  }
+  SsArgs a;
+  memset(&a, 0, sizeof(a));
+  a.res = static_cast<const __half*>(residual);
+  a.c = static_cast<__half*>(c);
+  a.err = error_flag;
+  a.M = (int)m;
+  a.N = (int)n;
+  a.K = (int)k;
+  a.rounds = (int)((k + kSgRoundK - 1) / kSgRoundK);
+  a.eps = eps;
+  a.cs0 = c_strides[0];
+  a.cs1 = c_strides[1];
+  if (residual) {
+    a.rs0 = residual_strides[0];
+    a.rs1 = residual_strides[1];
+  }
+  if (m <= 8)
+    return fold ? launch_small_gemm_stream<1, true>(st, tw, tx, a)
+                : launch_small_gemm_stream<1, false>(st, tw, tx, a);
+  return fold ? launch_small_gemm_stream<2, true>(st, tw, tx, a)
+              : launch_small_gemm_stream<2, false>(st, tw, tx, a);
+}
+
 }  // namespace fi
 
 extern "C" int fi_small_gemm(const void* x, const void* w, void* c, const void* residual,
@@ -294,6 +548,10 @@ extern "C" int fi_small_gemm(const void* x, const void* w, void* c, const void* 
     return fail(FI_ERR_ALIGNMENT,
                 "fi_small_gemm: x / w need 16-byte aligned bases, unit inner strides and row "
                 "strides that are multiples of 8 elements");
+  if (!norm_weight)  // x straight from global memory by TMA: the streamed variant
+    return small_gemm_streamed(x, w, c, residual, false, eps, m, n, k, x_strides, w_strides,
+                               c_strides, residual_strides, error_flag,
+                               static_cast<cudaStream_t>(stream));
   CUtensorMap tm;
   {
     const uint64_t dims[3] = {(uint64_t)kSgChunk, (uint64_t)n, (uint64_t)(k / kSgChunk)};
@@ -330,4 +588,32 @@ extern "C" int fi_small_gemm(const void* x, const void* w, void* c, const void* 
     return fail(FI_ERR_UNSUPPORTED, "fi_small_gemm: K too large to stage x in shared memory");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return nt == 1 ? launch_small_gemm<1>(st, tm, a, smem) : launch_small_gemm<2>(st, tm, a, smem);
+}
+
+extern "C" int fi_small_gemm_folded(const void* x, const void* w_folded, void* c,
+                                    const void* residual, float eps, int64_t m, int64_t n,
+                                    int64_t k, const int64_t* x_strides,
+                                    const int64_t* w_strides, const int64_t* c_strides,
+                                    const int64_t* residual_strides, int32_t* error_flag,
+                                    void* stream) {
+  using namespace fi;
+  clear_error();
+  if (m < 0 || n < 0 || k <= 0) return fail(FI_ERR_INVALID_ARG, "fi_small_gemm_folded: bad sizes");
+  if (m > kSgMaxM)
+    return fail(FI_ERR_UNSUPPORTED, "fi_small_gemm_folded: M (%lld) > %d", (long long)m, kSgMaxM);
+  if (k % kSgChunk != 0 || k > (1 << 20) || n > (1 << 30))
+    return fail(FI_ERR_UNSUPPORTED,
+                "fi_small_gemm_folded: K must be a multiple of 64 (and <= 2^20)");
+  if (m == 0 || n == 0) return FI_OK;
+  if (!x || !w_folded || !c || !x_strides || !w_strides || !c_strides ||
+      (residual && !residual_strides))
+    return fail(FI_ERR_INVALID_ARG, "fi_small_gemm_folded: null pointer argument");
+  if (x_strides[1] != 1 || x_strides[0] % 8 != 0 || !aligned16(x) || w_strides[1] != 1 ||
+      w_strides[0] % 8 != 0 || !aligned16(w_folded))
+    return fail(FI_ERR_ALIGNMENT,
+                "fi_small_gemm_folded: x / w need 16-byte aligned bases, unit inner strides and "
+                "row strides that are multiples of 8 elements");
+  return small_gemm_streamed(x, w_folded, c, residual, true, eps, m, n, k, x_strides, w_strides,
+                             c_strides, residual_strides, error_flag,
+                             static_cast<cudaStream_t>(stream));
 }

@@ -165,11 +165,12 @@ def fuse_qkv_inplace(weights: dict):
             mlp["gate_up_proj"] = cat([mlp.pop("gate_proj"), mlp.pop("up_proj")])
 
 
-# fi_small_gemm handles up to 16 rows; measured against the library GEMM (+ a separate
-# RMSNorm) on the Llama-3.2-3B attention projections it is faster up to 8 rows
-# (o projection at 1 row: 6.8 vs 11.7 us) and slower at 16 (QKV: 11.4 vs 9.2 us), so
-# larger batches take the library path.
+# fi_small_gemm handles up to 16 rows. With the exact RMSNorm prologue (x staged and
+# normalised by every CTA) it beats the library GEMM + RMSNorm launch up to 8 rows
+# and loses at 16 (QKV: 14.6 vs 12.3 us); without a norm x streams in by TMA with the
+# weight tiles (two CTAs per SM).
 SMALL_GEMM_MAX_M = 8
+STREAM_GEMM_MAX_M = 16
 
 
 def fp16_linear(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor = None,
@@ -201,7 +202,8 @@ def fp16_linear(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor = None,
     if out is None:
         out = torch.empty(*lead, N, dtype=torch.float16, device=x.device)
     o2 = out.view(-1, N)
-    if M <= SMALL_GEMM_MAX_M and K % 64 == 0 and M > 0 and N > 0:
+    limit = SMALL_GEMM_MAX_M if norm_weight is not None else STREAM_GEMM_MAX_M
+    if M <= limit and K % 64 == 0 and M > 0 and N > 0:
         if x2.stride(1) != 1 or x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
             x2 = x2.contiguous()
         if w.stride(1) != 1 or w.stride(0) % 8 != 0 or w.data_ptr() % 16 != 0:
@@ -229,4 +231,60 @@ def fp16_linear(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor = None,
         torch.addmm(r2, h, w.t(), out=o2) if o2.data_ptr() != r2.data_ptr() else o2.addmm_(h, w.t())
     else:
         torch.matmul(h, w.t(), out=o2)
+    return out
+
+
+def fold_rms_weight(w: torch.Tensor, norm_weight: torch.Tensor) -> torch.Tensor:
+    """w [N, K] with the RMSNorm weight folded in: fp16(w[n, k] * norm_weight[k]) (for
+    ``fp16_linear_folded``; prepared once per weight)."""
+    return (w.float() * norm_weight.float()[None, :]).half().contiguous()
+
+
+def fp16_linear_folded(x: torch.Tensor, w_folded: torch.Tensor, eps: float = 1e-5,
+                       residual: torch.Tensor = None, out: torch.Tensor = None) -> torch.Tensor:
+    """``residual + rsqrt(mean(x^2) + eps) * (x @ w_folded.T)`` = rms_norm(x) @ w.T with
+    the norm weight folded into ``w_folded`` (``fold_rms_weight``). Up to 16 rows: one
+    ``fi_small_gemm_folded`` launch (x streamed with the weight tiles, the per-row
+    factor applied in the epilogue); the rounding differs from the reference's
+    normalised-then-rounded x by fp16 noise. More rows: the same formula with library
+    ops."""
+    if not x.is_cuda or not w_folded.is_cuda:
+        raise ValueError("x and w must be CUDA tensors (fast_infer_b200 has no CPU path)")
+    if x.dtype != torch.float16 or w_folded.dtype != torch.float16:
+        raise TypeError("fp16_linear_folded expects float16 x and w")
+    K = x.shape[-1]
+    if w_folded.dim() != 2 or w_folded.shape[1] != K:
+        raise ValueError(f"w_folded must be [N, {K}]")
+    N = w_folded.shape[0]
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, K)
+    M = x2.shape[0]
+    r2 = residual.reshape(-1, N) if residual is not None else None
+    if out is None:
+        out = torch.empty(*lead, N, dtype=torch.float16, device=x.device)
+    o2 = out.view(-1, N)
+    if 0 < M <= STREAM_GEMM_MAX_M and K % 64 == 0 and N > 0:
+        if x2.stride(1) != 1 or x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
+            x2 = x2.contiguous()
+        w = w_folded
+        if w.stride(1) != 1 or w.stride(0) % 8 != 0 or w.data_ptr() % 16 != 0:
+            w = w.contiguous()
+        lib = _lib.load()
+        with with_device(x.device):
+            err = error_word(x.device)
+            st = lib.fi_small_gemm_folded(
+                x2.data_ptr(), w.data_ptr(), o2.data_ptr(),
+                r2.data_ptr() if r2 is not None else None, float(eps), M, N, K,
+                _lib.strides(*x2.stride()), _lib.strides(*w.stride()),
+                _lib.strides(*o2.stride()),
+                _lib.strides(*r2.stride()) if r2 is not None else None,
+                err.data_ptr() if err is not None else None, stream_of(x.device))
+            _lib.check(st, "fp16_linear_folded")
+            device_errors(err, "fp16_linear_folded")
+        return out
+    xf = x2.float()
+    y = (xf @ w_folded.float().t()) * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    if r2 is not None:
+        y = y + r2.float()
+    o2.copy_(y.half())
     return out

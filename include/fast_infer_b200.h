@@ -295,6 +295,20 @@ int fi_small_gemm(const void* x, const void* w, void* c, const void* residual,
                   const int64_t* residual_strides, int32_t* error_flag, void* stream);
 
 /*
+ * The same with the RMSNorm weight folded into the weights: w_folded[n, j] =
+ * fp16(w[n, j] * norm_weight[j]) (prepared once), and
+ *   c[i, :] = residual[i, :] + rsqrt(mean(x[i, :]^2) + eps) * (x[i, :] @ w_folded^T).
+ * Mathematically rmsnorm(x) @ w^T; the rounding differs from the reference's (the
+ * normalised x is not rounded to fp16, the folded weights are), within fp16 noise.
+ * x reaches the kernel by TMA with each weight tile instead of being staged and
+ * normalised first. Same layouts and limits as fi_small_gemm.
+ */
+int fi_small_gemm_folded(const void* x, const void* w_folded, void* c, const void* residual,
+                         float eps, int64_t m, int64_t n, int64_t k, const int64_t* x_strides,
+                         const int64_t* w_strides, const int64_t* c_strides,
+                         const int64_t* residual_strides, int32_t* error_flag, void* stream);
+
+/*
  * Head-output all-gather over NVLink peer memory, for a stack sharded by KV head.
  *
  * Replaces: the NCCL all-gather of per-rank attention outputs [rows, heads_r * 128]

@@ -147,3 +147,7 @@ def test_small_gemm_validation():
                              None, None) == _lib.FI_ERR_INVALID_ARG
     assert lib.fi_small_gemm(None, None, None, None, None, 1e-5, 0, 8, 64, s2, s2, s2, None,
                              None, None) == _lib.FI_OK
+    assert lib.fi_small_gemm_folded(None, None, None, None, 1e-5, 17, 8, 64, s2, s2, s2, None,
+                                    None, None) == _lib.FI_ERR_UNSUPPORTED
+    assert lib.fi_small_gemm_folded(None, None, None, None, 1e-5, 4, 8, 64, s2, s2, s2, None,
+                                    None, None) == _lib.FI_ERR_INVALID_ARG

@@ -15,12 +15,13 @@ def _kernel_up_to_16_rows(monkeypatch):
     """Route every size the kernel supports (up to 16 rows) through fi_small_gemm."""
     import fast_infer_b200.kernels.matmul as mm
     monkeypatch.setattr(mm, "SMALL_GEMM_MAX_M", 16)
+    monkeypatch.setattr(mm, "STREAM_GEMM_MAX_M", 16)
 
 
-def _close(out, ref):
+def _close(out, ref, abs_tol=1e-3, rel_tol=2.0 ** -10):
     out, ref = out.float(), ref.float()
     err = (out - ref).abs()
-    ok = bool((err <= 1e-3 + ref.abs() * 2.0 ** -10).all())
+    ok = bool((err <= abs_tol + ref.abs() * rel_tol).all())
     rel = float((out - ref).norm() / ref.norm().clamp_min(1e-30))
     return ok and rel <= 1e-3, float(err.max()), rel
 
@@ -78,3 +79,25 @@ def test_leading_dims_strides_and_fallback(cuda_device):
     big = fp16_linear(x4, w4, residual=r4, norm_weight=n4)
     ref = r4.float() + rms_norm(x4, n4).float() @ w4.float().t()
     assert _close(big, ref)[0]
+
+
+@pytest.mark.parametrize("m", [1, 7, 16])
+@pytest.mark.parametrize("n,k", [(2560, 3072), (5120, 3072), (100, 192)])
+def test_folded_norm(cuda_device, m, n, k):
+    """RMSNorm weight folded into the weights, per-row factor in the epilogue, against
+    rms_norm(x) @ w.T (+ residual) in fp32. Folding rounds every w * g to fp16 (where
+    the reference rounds the normalised x): one more fp16 rounding per product, so the
+    bound is max-abs 2e-3 + two fp16 ulps of the output, rel-L2 <= 1e-3."""
+    from fast_infer_b200.kernels.matmul import fold_rms_weight, fp16_linear_folded
+    x, w, res, nw = _data(m, n, k, cuda_device, m * 7 + n + k)
+    wf = fold_rms_weight(w, nw)
+    xf = x.float()
+    xn = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5) * nw.float()
+    ok = _close(fp16_linear_folded(x, wf), xn @ w.float().t(), 2e-3, 2.0 ** -9)
+    assert ok[0], ok
+    ok = _close(fp16_linear_folded(x, wf, residual=res), res.float() + xn @ w.float().t(),
+                2e-3, 2.0 ** -9)
+    assert ok[0], ok
+    h = res.clone()
+    fp16_linear_folded(x, wf, residual=h, out=h)
+    assert torch.equal(h, fp16_linear_folded(x, wf, residual=res))
