@@ -525,6 +525,7 @@ def run_stack(torch, dev, rank, world, dist, warmup=1):
     torch.cuda.synchronize()
     dec_ms = max_ms(e[0].elapsed_time(e[1]))
     finite = bool(torch.isfinite(h).all().item())
+    peer_errors = st._peer.errors() if st._peer is not None else 0
     st.close()
     sync_all()
     return {
@@ -540,6 +541,7 @@ def run_stack(torch, dev, rank, world, dist, warmup=1):
         "decode_tokens_per_s": round(STACK_BATCH * STACK_STEPS / (dec_ms * 1e-3), 1),
         "cuda_graph": use_graph,
         "finite": finite,
+        "peer_gather_errors": peer_errors,
     }
 
 

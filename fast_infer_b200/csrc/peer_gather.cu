@@ -83,6 +83,10 @@ __global__ void __launch_bounds__(kPgThreads) peer_gather_kernel(const PeerGathe
   for (int p = 0; p < a.world; ++p)
     st_release_sys(reinterpret_cast<uint32_t*>(a.base[p] + a.flags_off) + a.rank, e);
   const uint32_t* mine = reinterpret_cast<const uint32_t*>(a.base[a.rank] + a.flags_off);
+  // After one wait has run out (a peer gone or stuck) later calls do not wait again:
+  // a persistent error word turns a broken rendezvous into one 2 s delay, not one
+  // per call.
+  if (a.err && (*reinterpret_cast<volatile int*>(a.err) & FI_DEVERR_TIMEOUT)) return;
   const unsigned long long t0 = globaltimer_ns();
   for (int p = 0; p < a.world; ++p) {
     uint32_t spins = 0;

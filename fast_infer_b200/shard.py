@@ -151,6 +151,9 @@ class PeerGather:
         self._bases = (ctypes.c_void_p * 8)(*bases, *([None] * (8 - self.world)))
         self._buffers = torch.as_tensor(
             _DeviceArray(self._own, (nbuf, max_rows, self.world * row_elems)), device=self.device)
+        # persistent device error word of every gather (FI_DEVERR_TIMEOUT once a wait ran
+        # out; later gathers then skip their waits); read with ``errors()``
+        self._err = torch.zeros(1, dtype=torch.int32, device=self.device)
 
     def gather(self, local, buffer: int):
         import ctypes
@@ -160,15 +163,18 @@ class PeerGather:
         x = local.reshape(rows, self.row_elems)
         if x.stride(1) != 1 or (x.stride(0) * 2) % 16 != 0 or x.data_ptr() % 16 != 0:
             x = x.contiguous()
-        err = error_word(self.device)
         st = self._lib.fi_peer_gather(
             x.data_ptr(), rows, self.row_elems * 2, x.stride(0) * 2,
             ctypes.cast(self._bases, ctypes.POINTER(ctypes.c_void_p)), self.world, self.rank,
-            buffer, self.nbuf, self.max_rows, err.data_ptr() if err is not None else None,
-            stream_of(self.device))
+            buffer, self.nbuf, self.max_rows, self._err.data_ptr(), stream_of(self.device))
         _lib.check(st, "peer gather")
-        device_errors(err, "peer gather")
+        if error_word(self.device) is not None:  # device checks on: raise at once
+            device_errors(self._err, "peer gather")
         return self._buffers[buffer, :rows].view(*local.shape[:-1], self.world * self.row_elems)
+
+    def errors(self) -> int:
+        """FI_DEVERR_* bits raised by any gather so far (synchronises the stream)."""
+        return int(self._err.item())
 
     def close(self, group=None):
         """Unmap the peers' regions and free this rank's once every rank has unmapped

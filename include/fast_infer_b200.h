@@ -326,7 +326,9 @@ int fi_small_gemm_folded(const void* x, const void* w_folded, void* c, const voi
  * On return of the kernel this rank's buffer holds [rows, world * row_bytes] with rank
  * p's block at p. Calls are counted on the device, so a CUDA graph replays correctly;
  * every rank must make the same sequence of calls, and two uses of one buffer need
- * another gather between them. world <= 8.
+ * another gather between them. world <= 8. A call whose error_flag already holds
+ * FI_DEVERR_TIMEOUT does not wait (pass one persistent word to every call so a broken
+ * rendezvous costs one time-out).
  */
 size_t fi_peer_gather_bytes(int64_t nbuf, int64_t max_rows, int64_t row_total_bytes);
 int fi_peer_alloc(size_t bytes, void** ptr, void* handle);
