@@ -71,6 +71,10 @@ SIGNATURES = {
                                      _i64p, _i64p, _i64p, _vp, _vp]),
     "fi_small_gemm_folded": (ctypes.c_int, [_vp, _vp, _vp, _vp, _f32, _i64, _i64, _i64, _i64p,
                                             _i64p, _i64p, _i64p, _vp, _vp]),
+    "fi_qkv_rope_kv_write": (ctypes.c_int, [_vp, _vp, _f32, _i64, _i64, _i64, _i64, _i64, _i64p,
+                                            _i64p, _vp, _vp, _i64, _i64, _vp, _vp, _i64p, _vp,
+                                            _vp, _vp, _i64, _i64, _i64, _i64p, _i64p, _i64p,
+                                            _vp, _vp]),
     "fi_peer_gather_bytes": (_sz, [_i64, _i64, _i64]),
     "fi_peer_alloc": (ctypes.c_int, [_sz, ctypes.POINTER(_vp), _vp]),
     "fi_peer_open": (ctypes.c_int, [_vp, ctypes.POINTER(_vp)]),

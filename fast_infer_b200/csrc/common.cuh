@@ -38,6 +38,15 @@ __device__ __forceinline__ uint8_t* smem_align1024(uint8_t* raw) {
   return raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u);
 }
 
+// One output of the reference's RoPE in fp16 tensor arithmetic (kernels/rope.py:26-44):
+// fp16(fp16(x * c) + fp16(partner * s)), partner = -x_hi for the first half of a head
+// and x_lo for the second (rotate_half), every product and sum rounded as PyTorch does.
+__device__ __forceinline__ __half rope_elem(float x, float partner_signed, __half c, __half s) {
+  const __half a = __float2half_rn(x * __half2float(c));
+  const __half b = __float2half_rn(partner_signed * __half2float(s));
+  return __float2half_rn(__half2float(a) + __half2float(b));
+}
+
 __device__ __forceinline__ void set_error(int* err, int code) {
   if (err) atomicOr(err, code);
 }

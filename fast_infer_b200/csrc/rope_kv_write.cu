@@ -35,12 +35,6 @@ struct RopeArgs {
   int64_t xs[3], qs[4], ks[4], kcs[4], vcs[4], bts[2], tab_stride;
 };
 
-__device__ __forceinline__ __half rope_elem(float x, float partner_signed, __half c, __half s) {
-  const __half a = __float2half_rn(x * __half2float(c));
-  const __half b = __float2half_rn(partner_signed * __half2float(s));
-  return __float2half_rn(__half2float(a) + __half2float(b));
-}
-
 __global__ void __launch_bounds__(256) rope_kv_write_kernel(const RopeArgs a) {
   grid_dep_wait();
   grid_dep_launch();

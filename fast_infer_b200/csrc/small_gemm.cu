@@ -288,6 +288,18 @@ struct SsArgs {
   int M, N, K, rounds;
   float eps;
   int64_t cs0, cs1, rs0, rs1;
+  // kRope epilogue: RoPE of q / k and the KV-cache slot writes of k / v (one token per
+  // sequence; row m of x is sequence m at position start_pos[m])
+  const float* cos_tab;
+  const float* sin_tab;
+  const int32_t* start_pos;
+  __half* q_out;
+  __half* kc;
+  __half* vc;
+  const int32_t* bt;
+  int nq, nkv;
+  int64_t max_pos, tab_stride, num_blocks, block_size, max_blocks;
+  int64_t qs[3], kcs[4], vcs[4], bts[2];
 };
 
 template <int NT>
@@ -296,7 +308,7 @@ __host__ __device__ constexpr size_t ss_smem_bytes() {
          (size_t)kSgWarps * 16 * 4 + 16 * 4;
 }
 
-template <int NT, bool kFold>
+template <int NT, bool kFold, bool kRope>
 __global__ void __launch_bounds__(kSgThreads, 2)
     small_gemm_stream_kernel(const __grid_constant__ CUtensorMap tm_w,
                              const __grid_constant__ CUtensorMap tm_x, const SsArgs a) {
@@ -436,23 +448,82 @@ __global__ void __launch_bounds__(kSgThreads, 2)
       }
     }
     named_bar_sync(kSgBar, kSgWarps * 32);
-    const int nbase = item * kSgRows;
-    for (int i = tid; i < a.M * kSgRows; i += kSgWarps * 32) {
-      const int m = i / kSgRows, rr = i - m * kSgRows, n = nbase + rr;
-      float sum = 0.f;
+    if constexpr (kRope) {
+      // Weight rows are permuted so that item 8h + ci holds dims ci*8 .. ci*8+7 of
+      // head h in rows 0-7 and dims 64 + ci*8 .. in rows 8-15: each thread takes one
+      // rotary pair (d, d + 64) of one token, rounds both projection outputs to fp16
+      // (the values the unfused path stores) and applies the reference's RoPE and
+      // slot writes to them (as fi_rope_kv_write does).
+      const int head = item >> 3, ci = item & 7;
+      for (int i = tid; i < a.M * 8; i += kSgWarps * 32) {
+        const int m = i >> 3, rr = i & 7;
+        float lo = 0.f, hi = 0.f;
 #pragma unroll
-      for (int w = 0; w < kSgWarps; ++w) sum += red[w][m][rr];
-      if (kFold) sum *= rmsv[m];
-      if (n < a.N) {
-        if (a.res) sum += __half2float(a.res[m * a.rs0 + n * a.rs1]);
-        a.c[m * a.cs0 + n * a.cs1] = __float2half_rn(sum);
+        for (int w = 0; w < kSgWarps; ++w) {
+          lo += red[w][m][rr];
+          hi += red[w][m][rr + 8];
+        }
+        if (kFold) {
+          lo *= rmsv[m];
+          hi *= rmsv[m];
+        }
+        __half ol = __float2half_rn(lo), oh = __float2half_rn(hi);
+        const int d0 = ci * 8 + rr, d1 = 64 + d0;
+        const int64_t pos = a.start_pos[m];
+        const bool is_v = head >= a.nq + a.nkv;
+        if (!is_v) {
+          if (pos < 0 || pos >= a.max_pos) {
+            set_error(a.err, FI_DEVERR_CONTEXT_LEN);
+            continue;
+          }
+          const float* ct = a.cos_tab + pos * a.tab_stride;
+          const float* sn = a.sin_tab + pos * a.tab_stride;
+          const float xlo = __half2float(ol), xhi = __half2float(oh);
+          ol = rope_elem(xlo, -xhi, __float2half_rn(ct[d0]), __float2half_rn(sn[d0]));
+          oh = rope_elem(xhi, xlo, __float2half_rn(ct[d1]), __float2half_rn(sn[d1]));
+        }
+        if (head < a.nq) {
+          __half* dst = a.q_out + m * a.qs[0] + head * a.qs[1];
+          dst[d0 * a.qs[2]] = ol;
+          dst[d1 * a.qs[2]] = oh;
+          continue;
+        }
+        const int kvh = is_v ? head - a.nq - a.nkv : head - a.nq;
+        const int64_t lblk = pos / a.block_size;
+        if (pos < 0 || lblk >= a.max_blocks) {
+          set_error(a.err, FI_DEVERR_BAD_BLOCK);
+          continue;
+        }
+        const int64_t phys = a.bt[m * a.bts[0] + lblk * a.bts[1]];
+        if (phys < 0 || phys >= a.num_blocks) {
+          set_error(a.err, FI_DEVERR_BAD_BLOCK);
+          continue;
+        }
+        const int64_t slot = pos % a.block_size;
+        const int64_t* cs = is_v ? a.vcs : a.kcs;
+        __half* dst = (is_v ? a.vc : a.kc) + phys * cs[0] + slot * cs[1] + kvh * cs[2];
+        dst[d0 * cs[3]] = ol;
+        dst[d1 * cs[3]] = oh;
+      }
+    } else {
+      const int nbase = item * kSgRows;
+      for (int i = tid; i < a.M * kSgRows; i += kSgWarps * 32) {
+        const int m = i / kSgRows, rr = i - m * kSgRows, n = nbase + rr;
+        float sum = 0.f;
+#pragma unroll
+        for (int w = 0; w < kSgWarps; ++w) sum += red[w][m][rr];
+        if (kFold) sum *= rmsv[m];
+        if (n < a.N) {
+          if (a.res) sum += __half2float(a.res[m * a.rs0 + n * a.rs1]);
+          a.c[m * a.cs0 + n * a.cs1] = __float2half_rn(sum);
+        }
       }
     }
     named_bar_sync(kSgBar, kSgWarps * 32);
   }
 }
 
-template <int NT, bool kFold>
+template <int NT, bool kFold, bool kRope = false>
 static int launch_small_gemm_stream(cudaStream_t st, const CUtensorMap& tw, const CUtensorMap& tx,
                                     const SsArgs& a) {
   static bool attr_done[64] = {false};
@@ -461,22 +532,41 @@ static int launch_small_gemm_stream(cudaStream_t st, const CUtensorMap& tw, cons
   if (dev < 0 || dev >= 64) dev = 0;
   constexpr size_t smem = ss_smem_bytes<NT>();
   if (!attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(small_gemm_stream_kernel<NT, kFold>,
+    cudaError_t e = cudaFuncSetAttribute(small_gemm_stream_kernel<NT, kFold, kRope>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_fail(e, "fi_small_gemm: cudaFuncSetAttribute");
     attr_done[dev] = true;
   }
   int nb = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, small_gemm_stream_kernel<NT, kFold>,
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, small_gemm_stream_kernel<NT, kFold, kRope>,
                                                     kSgThreads, smem) != cudaSuccess || nb < 1)
     nb = 1;
   const int items = (a.N + kSgRows - 1) / kSgRows;
   int grid = nb * sm_count();
   if (grid > items) grid = items;
-  cudaError_t e = launch_pdl(small_gemm_stream_kernel<NT, kFold>, dim3((unsigned)grid),
+  cudaError_t e = launch_pdl(small_gemm_stream_kernel<NT, kFold, kRope>, dim3((unsigned)grid),
                              dim3(kSgThreads), smem, st, tw, tx, a);
   if (e != cudaSuccess) return cuda_fail(e, "fi_small_gemm launch");
   return FI_OK;
+}
+
+// Tensor maps of the streamed variant: w [n, k] and x [m, k] as (64-element chunk
+// column, row, chunk) with 16-row x 8-chunk boxes, 128B swizzle.
+static int stream_maps(const void* x, const void* w, int64_t m, int64_t n, int64_t k,
+                       const int64_t* x_strides, const int64_t* w_strides, CUtensorMap* tw,
+                       CUtensorMap* tx) {
+  const uint32_t box[3] = {(uint32_t)kSgChunk, (uint32_t)kSgRows, (uint32_t)kSgWarps};
+  {
+    const uint64_t dims[3] = {(uint64_t)kSgChunk, (uint64_t)n, (uint64_t)(k / kSgChunk)};
+    const uint64_t sb[2] = {(uint64_t)w_strides[0] * 2, 128};
+    const int r = encode_tiled(tw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, w, dims, sb, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B, "fi_small_gemm w");
+    if (r != FI_OK) return r;
+  }
+  const uint64_t dims[3] = {(uint64_t)kSgChunk, (uint64_t)m, (uint64_t)(k / kSgChunk)};
+  const uint64_t sb[2] = {(uint64_t)x_strides[0] * 2, 128};
+  return encode_tiled(tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, x, dims, sb, box,
+                      CU_TENSOR_MAP_SWIZZLE_128B, "fi_small_gemm x");
 }
 
 // Tensor maps and launch of the streamed variant (x [m, k] and w [n, k] already
@@ -487,19 +577,8 @@ static int small_gemm_streamed(const void* x, const void* w, void* c, const void
                                const int64_t* c_strides, const int64_t* residual_strides,
                                int32_t* error_flag, cudaStream_t st) {
   CUtensorMap tw, tx;
-  const uint32_t box[3] = {(uint32_t)kSgChunk, (uint32_t)kSgRows, (uint32_t)kSgWarps};
   {
-    const uint64_t dims[3] = {(uint64_t)kSgChunk, (uint64_t)n, (uint64_t)(k / kSgChunk)};
-    const uint64_t sb[2] = {(uint64_t)w_strides[0] * 2, 128};
-    const int r = encode_tiled(&tw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, w, dims, sb, box,
-                               CU_TENSOR_MAP_SWIZZLE_128B, "fi_small_gemm w");
-    if (r != FI_OK) return r;
-  }
-  {
-    const uint64_t dims[3] = {(uint64_t)kSgChunk, (uint64_t)m, (uint64_t)(k / kSgChunk)};
-    const uint64_t sb[2] = {(uint64_t)x_strides[0] * 2, 128};
-    const int r = encode_tiled(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, x, dims, sb, box,
-                               CU_TENSOR_MAP_SWIZZLE_128B, "fi_small_gemm x");
+    const int r = stream_maps(x, w, m, n, k, x_strides, w_strides, &tw, &tx);
     if (r != FI_OK) return r;
   }
   SsArgs a;
@@ -616,4 +695,75 @@ extern "C" int fi_small_gemm_folded(const void* x, const void* w_folded, void* c
   return small_gemm_streamed(x, w_folded, c, residual, true, eps, m, n, k, x_strides, w_strides,
                              c_strides, residual_strides, error_flag,
                              static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fi_qkv_rope_kv_write(
+    const void* x, const void* w_rope, float eps, int64_t batch, int64_t k, int64_t num_q_heads,
+    int64_t num_kv_heads, int64_t head_dim, const int64_t* x_strides, const int64_t* w_strides,
+    const float* cos_table, const float* sin_table, int64_t table_rows, int64_t table_stride,
+    const int32_t* start_pos, void* q_out, const int64_t* q_out_strides, void* k_cache,
+    void* v_cache, const int32_t* block_table, int64_t num_blocks, int64_t block_size,
+    int64_t max_blocks_per_seq, const int64_t* kc_strides, const int64_t* vc_strides,
+    const int64_t* bt_strides, int32_t* error_flag, void* stream) {
+  using namespace fi;
+  clear_error();
+  if (batch < 0 || k <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || block_size <= 0 ||
+      num_blocks <= 0 || max_blocks_per_seq <= 0 || table_rows <= 0)
+    return fail(FI_ERR_INVALID_ARG, "fi_qkv_rope_kv_write: bad sizes");
+  if (head_dim != 128)
+    return fail(FI_ERR_UNSUPPORTED, "fi_qkv_rope_kv_write: head_dim %lld != 128",
+                (long long)head_dim);
+  if (batch > kSgMaxM)
+    return fail(FI_ERR_UNSUPPORTED, "fi_qkv_rope_kv_write: batch (%lld) > %d", (long long)batch,
+                kSgMaxM);
+  if (k % kSgChunk != 0 || k > (1 << 20))
+    return fail(FI_ERR_UNSUPPORTED, "fi_qkv_rope_kv_write: K must be a multiple of 64");
+  if (batch == 0) return FI_OK;
+  if (!x || !w_rope || !cos_table || !sin_table || !start_pos || !q_out || !k_cache ||
+      !v_cache || !block_table || !x_strides || !w_strides || !q_out_strides || !kc_strides ||
+      !vc_strides || !bt_strides)
+    return fail(FI_ERR_INVALID_ARG, "fi_qkv_rope_kv_write: null pointer argument");
+  if (x_strides[1] != 1 || x_strides[0] % 8 != 0 || !aligned16(x) || w_strides[1] != 1 ||
+      w_strides[0] % 8 != 0 || !aligned16(w_rope))
+    return fail(FI_ERR_ALIGNMENT,
+                "fi_qkv_rope_kv_write: x / w need 16-byte aligned bases, unit inner strides and "
+                "row strides that are multiples of 8 elements");
+  const int64_t n = (num_q_heads + 2 * num_kv_heads) * head_dim;
+  CUtensorMap tw, tx;
+  {
+    const int r = stream_maps(x, w_rope, batch, n, k, x_strides, w_strides, &tw, &tx);
+    if (r != FI_OK) return r;
+  }
+  SsArgs a;
+  memset(&a, 0, sizeof(a));
+  a.err = error_flag;
+  a.M = (int)batch;
+  a.N = (int)n;
+  a.K = (int)k;
+  a.rounds = (int)((k + kSgRoundK - 1) / kSgRoundK);
+  a.eps = eps;
+  a.cos_tab = cos_table;
+  a.sin_tab = sin_table;
+  a.start_pos = start_pos;
+  a.q_out = static_cast<__half*>(q_out);
+  a.kc = static_cast<__half*>(k_cache);
+  a.vc = static_cast<__half*>(v_cache);
+  a.bt = block_table;
+  a.nq = (int)num_q_heads;
+  a.nkv = (int)num_kv_heads;
+  a.max_pos = table_rows;
+  a.tab_stride = table_stride;
+  a.num_blocks = num_blocks;
+  a.block_size = block_size;
+  a.max_blocks = max_blocks_per_seq;
+  for (int i = 0; i < 3; ++i) a.qs[i] = q_out_strides[i];
+  for (int i = 0; i < 4; ++i) {
+    a.kcs[i] = kc_strides[i];
+    a.vcs[i] = vc_strides[i];
+  }
+  a.bts[0] = bt_strides[0];
+  a.bts[1] = bt_strides[1];
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return batch <= 8 ? launch_small_gemm_stream<1, true, true>(st, tw, tx, a)
+                    : launch_small_gemm_stream<2, true, true>(st, tw, tx, a);
 }

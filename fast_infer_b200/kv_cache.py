@@ -299,3 +299,64 @@ def rope_and_store(cache: KVCache, layer_idx: int, qkv: torch.Tensor, num_q_head
         _lib.check(st, "rope_and_store")
         device_errors(err, "rope_and_store")
     return q_out
+
+
+def permute_rope_rows(w: torch.Tensor, head_dim: int = 128) -> torch.Tensor:
+    """Rows of a QKV weight [heads * head_dim, K] reordered for ``qkv_rope_store``:
+    within each head, 16-row tiles of dims (8c .. 8c+7, 64+8c .. 64+8c+7), c = 0..7,
+    so every tile holds its rotary pairs (d, d + 64)."""
+    if head_dim != 128 or w.shape[0] % head_dim != 0:
+        raise ValueError("permute_rope_rows expects head_dim 128 and whole heads")
+    heads = w.shape[0] // head_dim
+    base = torch.arange(8).repeat_interleave(8) * 8 + torch.arange(8).repeat(8)  # 8c + r
+    tile = torch.stack([base.view(8, 8), base.view(8, 8) + 64], dim=1).reshape(-1)
+    idx = (torch.arange(heads)[:, None] * head_dim + tile[None, :]).reshape(-1)
+    return w[idx.to(w.device)].contiguous()
+
+
+def qkv_rope_store(cache: KVCache, layer_idx: int, x: torch.Tensor, w_rope: torch.Tensor,
+                   num_q_heads: int, cos_table: torch.Tensor, sin_table: torch.Tensor,
+                   start_pos: torch.Tensor, eps: float = 1e-5,
+                   q_out: torch.Tensor = None) -> torch.Tensor:
+    """Decode step, one launch: RMSNorm + QKV projection + RoPE + KV slot writes.
+
+    x: [B, 1, K] or [B, K] fp16 (one new token per sequence, B <= 16); w_rope: the
+    folded QKV weight (``kernels.matmul.fold_rms_weight``) with rows permuted by
+    ``permute_rope_rows``; start_pos: [B] int32 device positions. The same bits as
+    ``fp16_linear_folded`` followed by ``rope_and_store``. Returns rotated q
+    [B, 1, nq, D] (``q_out`` if given).
+    """
+    cache.sync_block_table()
+    D, nkv = cache.head_dim, cache.num_heads
+    x2 = x.reshape(-1, x.shape[-1])
+    B, K = x2.shape
+    if x2.dtype != torch.float16 or x2.device != cache.device:
+        raise ValueError("x must be float16 on the cache device")
+    if w_rope.shape != ((num_q_heads + 2 * nkv) * D, K):
+        raise ValueError("w_rope must be [(nq + 2*nkv) * head_dim, K]")
+    if B > cache.block_table.shape[0]:
+        raise ValueError("batch larger than the block table; call _grow_batch first")
+    if not isinstance(start_pos, torch.Tensor) or start_pos.numel() != B:
+        raise ValueError("start_pos must be a [B] device tensor")
+    if x2.stride(1) != 1 or x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
+        x2 = x2.contiguous()
+    sp = start_pos.to(torch.int32).contiguous()
+    if q_out is None:
+        q_out = torch.empty(B, 1, num_q_heads, D, dtype=torch.float16, device=cache.device)
+    q2 = q_out[:, 0]
+    kc, vc = cache.k[layer_idx], cache.v[layer_idx]
+    lib = _lib.load()
+    with with_device(cache.device):
+        err = error_word(cache.device)
+        st = lib.fi_qkv_rope_kv_write(
+            x2.data_ptr(), w_rope.data_ptr(), float(eps), B, K, num_q_heads, nkv, D,
+            _lib.strides(*x2.stride()), _lib.strides(*w_rope.stride()),
+            cos_table.data_ptr(), sin_table.data_ptr(), cos_table.shape[0], cos_table.stride(0),
+            sp.data_ptr(), q2.data_ptr(), _lib.strides(*q2.stride()),
+            kc.data_ptr(), vc.data_ptr(), cache.block_table.data_ptr(), cache.num_blocks,
+            cache.block_size, cache.max_blocks_per_seq, _lib.strides(*kc.stride()),
+            _lib.strides(*vc.stride()), _lib.strides(*cache.block_table.stride()),
+            err.data_ptr() if err is not None else None, stream_of(cache.device))
+        _lib.check(st, "qkv_rope_store")
+        device_errors(err, "qkv_rope_store")
+    return q_out

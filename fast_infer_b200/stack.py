@@ -36,9 +36,9 @@ import torch
 
 from fast_infer_b200._runtime import device_checks
 from fast_infer_b200.kernels.attention import flash_attention, paged_attention
-from fast_infer_b200.kernels.matmul import fold_rms_weight, fp16_linear, fp16_linear_folded
+from fast_infer_b200.kernels.matmul import fold_rms_weight, fp16_linear
 from fast_infer_b200.kernels.rms_norm import rms_norm
-from fast_infer_b200.kv_cache import KVCache, rope_and_store
+from fast_infer_b200.kv_cache import KVCache, permute_rope_rows, qkv_rope_store, rope_and_store
 from fast_infer_b200.shard import HeadShard, PeerGather, gather_heads, head_shard
 
 
@@ -104,8 +104,11 @@ class AttentionStack:
             # weights kept as [out, in] (the reference's linear layout): the decode GEMMs
             # stream them row by row, the prefill GEMMs read them transposed
             wqkv_t = wqkv.t().half().contiguous()
+            # decode: norm weight folded in, rows permuted so each 16-row tile holds
+            # its rotary pairs (one launch for norm + QKV + RoPE + slot writes)
             self.layers.append(dict(norm=norm.half(), wqkv_t=wqkv_t,
-                                    wqkv_fold=fold_rms_weight(wqkv_t, norm.half()),
+                                    wqkv_rope=permute_rope_rows(
+                                        fold_rms_weight(wqkv_t, norm.half())),
                                     wo_t=wo.t().half().contiguous()))
         self.cos, self.sin = precompute_freqs(head_dim, max_seq_len, rope_theta, self.device)
         pages_per_seq = (max_seq_len + 63) // 64
@@ -186,10 +189,9 @@ class AttentionStack:
         span = self.cache.max_blocks_per_seq * 64
         h = self._h_in.clone()  # the residual stream is updated in place below
         for li, w in enumerate(self.layers):
-            # RMSNorm + QKV projection in one launch (norm weight folded into the
-            # weights, per-token factor in the GEMM epilogue)
-            qkv = fp16_linear_folded(h, w["wqkv_fold"], eps=self.eps)
-            q = rope_and_store(self.cache, li, qkv, nq, self.cos, self.sin, self._dev_start)
+            # RMSNorm + QKV projection + RoPE + KV slot writes in one launch
+            q = qkv_rope_store(self.cache, li, h, w["wqkv_rope"], nq, self.cos, self.sin,
+                               self._dev_start, eps=self.eps)
             o = paged_attention(q[:, 0], self.cache.k[li], self.cache.v[li],
                                 self.cache.block_table, 64, 0, context_lens=self._dev_ctx,
                                 max_context_len=span, workspace=self._ws)

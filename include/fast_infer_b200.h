@@ -309,6 +309,34 @@ int fi_small_gemm_folded(const void* x, const void* w_folded, void* c, const voi
                          const int64_t* residual_strides, int32_t* error_flag, void* stream);
 
 /*
+ * Decode-step QKV projection with RMSNorm, RoPE and the KV-cache slot writes in one
+ * launch: for each sequence b (< batch <= 16; one token each, row b of x [batch, k])
+ *   qkv = rsqrt(mean(x[b]^2) + eps) * (x[b] @ w^T)  rounded to fp16,
+ * then RoPE of the q and k heads at position start_pos[b] and the writes, exactly as
+ * fi_rope_kv_write does with that qkv: rotated q to q_out [batch, nq, 128] (strides: 3
+ * entries), rotated k and raw v to page block_table[b, pos / block_size], row
+ * pos % block_size of k_cache / v_cache (layouts as in fi_kv_write).
+ * w_rope is the folded weight of fi_small_gemm_folded ([(nq + 2 nkv) * 128, k]) with
+ * its rows permuted per head: for head h and c in 0..7, rows 128h + 16c .. +7 hold
+ * dims 8c .. 8c+7 and rows 128h + 16c + 8 .. +15 hold dims 64 + 8c .. (so each
+ * 16-row tile carries its rotary pairs). head_dim 128; cos/sin fp32 [table_rows,
+ * table_stride].
+ *
+ * Replaces, at decode batch sizes: the RMSNorm + QKV projection (model.py:82-93) and
+ * the RoPE + slot writes (kernels/rope.py:26-44, model.py:101,185-201).
+ */
+int fi_qkv_rope_kv_write(const void* x, const void* w_rope, float eps, int64_t batch, int64_t k,
+                         int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
+                         const int64_t* x_strides, const int64_t* w_strides,
+                         const float* cos_table, const float* sin_table, int64_t table_rows,
+                         int64_t table_stride, const int32_t* start_pos, void* q_out,
+                         const int64_t* q_out_strides, void* k_cache, void* v_cache,
+                         const int32_t* block_table, int64_t num_blocks, int64_t block_size,
+                         int64_t max_blocks_per_seq, const int64_t* kc_strides,
+                         const int64_t* vc_strides, const int64_t* bt_strides,
+                         int32_t* error_flag, void* stream);
+
+/*
  * Head-output all-gather over NVLink peer memory, for a stack sharded by KV head.
  *
  * Replaces: the NCCL all-gather of per-rank attention outputs [rows, heads_r * 128]
