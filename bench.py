@@ -76,11 +76,12 @@ def make_tables(lens, rng):
     return bt, total
 
 
-def decode_bytes(lens):
-    """Algorithmic HBM bytes of one decode pass: every K and V byte once (fp16),
-    Q and O (fp16) and one int32 block-table entry per page."""
+def decode_bytes(lens, hkv=HKV):
+    """Algorithmic HBM bytes of one decode pass over ``hkv`` KV heads (and their 3x
+    query heads): every K and V byte once (fp16), Q and O (fp16) and one int32
+    block-table entry per page."""
     lens = np.asarray(lens, np.int64)
-    return float(lens.sum() * HKV * D * 4 + len(lens) * HQ * D * 4 +
+    return float(lens.sum() * hkv * D * 4 + len(lens) * 3 * hkv * D * 4 +
                  sum(math.ceil(int(n) / BS) for n in lens) * 4)
 
 
@@ -139,7 +140,7 @@ class ClockSampler:
 
 # --------------------------------------------------------------- our arm
 class DecodeWorkload:
-    def __init__(self, torch, dev, n_seqs, lo, hi, seed, layers):
+    def __init__(self, torch, dev, n_seqs, lo, hi, seed, layers, hkv=HKV):
         rng = np.random.default_rng(seed + 1000)
         self.lens = ragged_lens(n_seqs, lo, hi, seed)
         # the step's new token sits at position len-1 (already counted in lens)
@@ -149,7 +150,8 @@ class DecodeWorkload:
         self.layers = layers
         g = torch.Generator(device=dev)
         g.manual_seed(seed)
-        self.k = torch.empty(layers, total, BS, HKV, D, dtype=torch.float16, device=dev)
+        self.hkv, self.hq = hkv, 3 * hkv
+        self.k = torch.empty(layers, total, BS, hkv, D, dtype=torch.float16, device=dev)
         self.v = torch.empty_like(self.k)
         for l in range(layers):
             self.k[l].normal_(generator=g)
@@ -157,13 +159,13 @@ class DecodeWorkload:
         self.bt = torch.from_numpy(bt).to(dev)
         self.ctx = torch.from_numpy(self.lens).to(dev)
         self.start = (self.ctx - 1).contiguous()
-        self.q = torch.randn(n_seqs, HQ, D, device=dev, generator=g).half()
-        self.kn = torch.randn(n_seqs, 1, HKV, D, device=dev, generator=g).half()
-        self.vn = torch.randn(n_seqs, 1, HKV, D, device=dev, generator=g).half()
+        self.q = torch.randn(n_seqs, self.hq, D, device=dev, generator=g).half()
+        self.kn = torch.randn(n_seqs, 1, hkv, D, device=dev, generator=g).half()
+        self.vn = torch.randn(n_seqs, 1, hkv, D, device=dev, generator=g).half()
         self.max_ctx = int(self.lens.max())
-        self.bytes = decode_bytes(self.lens)
+        self.bytes = decode_bytes(self.lens, hkv)
         from fast_infer_b200.kernels.attention import paged_attention_workspace_bytes
-        need = paged_attention_workspace_bytes(n_seqs, HQ, HKV, self.max_ctx)
+        need = paged_attention_workspace_bytes(n_seqs, self.hq, hkv, self.max_ctx)
         self.ws = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
 
     def attend(self, layer, q=None):
@@ -180,7 +182,7 @@ class DecodeWorkload:
         kc, vc = self.k[layer], self.v[layer]
         st = load().fi_kv_write(
             kn.data_ptr(), vn.data_ptr(), kc.data_ptr(), vc.data_ptr(), self.bt.data_ptr(),
-            self.start.data_ptr(), 0, None, kn.shape[0], 1, HKV, D, kc.shape[0], BS,
+            self.start.data_ptr(), 0, None, kn.shape[0], 1, self.hkv, D, kc.shape[0], BS,
             self.bt.shape[1], strides(*kn.stride()), strides(*vn.stride()),
             strides(*kc.stride()), strides(*vc.stride()), strides(*self.bt.stride()), None,
             torch.cuda.current_stream().cuda_stream)
@@ -324,6 +326,24 @@ def run_ours(args):
     wl3 = DecodeWorkload(torch, dev, C3_SEQS, C3_LO, C3_HI, C3_SEED + rank, 8)
     ms3 = timed(torch, lambda i: wl3.attend(i % 8), args.steps, args.warmup, dist) / args.steps
     c3_gbs = wl3.bytes / (ms3 * 1e-3) / 1e9
+    del wl3
+
+    # ---- config 5 partitioned by KV head: every rank owns 8/N KV heads (and their
+    # query heads) of the same 256 sequences (seed 3 on every rank); no collective;
+    # strong scaling. 4 resident layers rotated (each > L2 up to N = 8).
+    kvh = None
+    if HKV % world == 0:
+        wl5 = DecodeWorkload(torch, dev, DECODE_SEQS, DECODE_LO, DECODE_HI, DECODE_SEED, 4,
+                             hkv=HKV // world)
+        ms5 = timed(torch, lambda i: wl5.attend(i % 4), args.steps, args.warmup, dist) / args.steps
+        gbs5 = wl5.bytes * world / (ms5 * 1e-3) / 1e9
+        kvh = {"workload": "config 5: 256 seqs, ctx U[1024,4096] (seed 3), GQA 24/8, KV heads "
+                           f"sharded {HKV // world} per GPU over {world} GPU(s), paged decode "
+                           "(+ combine), 4 layers rotated",
+               "scaling": "strong", "ms": round(ms5, 4), "gbs": round(gbs5, 1),
+               "frac_per_gpu": round(gbs5 / world / hbm_peak, 4),
+               "tokens_per_s": round(DECODE_SEQS / (ms5 * 1e-3), 1)}
+        del wl5
 
     stack = run_stack(torch, dev, rank, world, dist) if not args.no_stack else None
     int4 = run_int4(torch, dev, max(args.steps // 8, 20), args.warmup, hbm_peak,
@@ -374,6 +394,7 @@ def run_ours(args):
             "ms": round(ms3, 4), "gbs": round(c3_gbs, 1),
             "frac": round(c3_gbs / hbm_peak, 4),
         },
+        "decode_kv_head_sharded": kvh,
         "stack": stack,
         "int4_gemm": int4,
         "e2e": {

@@ -114,7 +114,7 @@ def test_small_grids_two_page_groups(cuda_device, device_checks, batch, hq, hkv,
     _ok(outs[0].cpu().numpy(), paged_attention_fp32(q, kc, vc, bt, lens))
 
 
-@pytest.mark.parametrize("hq,hkv", [(8, 8), (32, 4), (24, 8), (4, 2)])
+@pytest.mark.parametrize("hq,hkv", [(8, 8), (32, 4), (24, 8), (4, 2), (3, 1), (6, 2), (12, 4)])
 def test_gqa_group_sizes(cuda_device, device_checks, hq, hkv):
     from fast_infer_b200.kernels.attention import paged_attention
     rng = np.random.default_rng(hq * 10 + hkv)
