@@ -3,21 +3,23 @@
 // Replaces, for the decode step of a KV-head-sharded stack, the NCCL all-gather of
 // the per-rank head outputs before the replicated O projection (the one exchange of
 // the sharded path, model.py:123-134 run with heads split over GPUs). One kernel per
-// gather writes this rank's [rows, row_bytes] block straight into every rank's
-// gather buffer (plain 16-byte stores through the peer mapping, NVLink), then
-// raises this rank's flag in every peer and waits (bounded) until every peer's flag
-// for the same call has arrived: no library collective, no host involvement, one
-// launch, CUDA-graph capturable.
+// gather, no library collective, no host involvement, CUDA-graph capturable.
+//
+// Protocol: flags travel inside the data. Every 4-byte word of this rank's rows is
+// sent to every rank as one 8-byte store {word, epoch} (an 8-byte store reaches the
+// peer whole), so no system-scope fence is needed: each rank polls the words of its
+// own landing area until every word carries the current call's epoch, unpacking
+// them into its output rows. The epoch counts calls on the device, so a replayed
+// graph matches calls across ranks, and a stale word (an older call) never passes.
 //
 // Each rank owns one region (fi_peer_alloc, shared with the others through
 // cudaIpcGetMemHandle / cudaIpcOpenMemHandle):
-//   [nbuf gather buffers: nbuf x max_rows x row_total bytes]
-//   [flags: 64 x uint32, flags[p] = number of gathers rank p has delivered here]
-//   [local: epoch (gathers done by this rank), CTA arrival counter]
-// Calls are counted on the device (epoch), so a replayed graph waits for the
-// matching call of every peer. A buffer must not be rewritten while a peer may still
-// read it: callers rotate buffers so that two uses of one buffer have another
-// gather between them (the stack uses one buffer per layer).
+//   [output: nbuf buffers x max_rows x row_total bytes]   (row_total = world x row)
+//   [landing area: nbuf x max_rows x world x row words, 8 bytes each]
+//   [local: epoch (calls made by this rank), CTA arrival counter]
+// A buffer must not be rewritten while a peer may still read it: callers rotate
+// buffers so that two uses of one buffer have another gather between them (the
+// stack uses one buffer per layer).
 #include <cuda_runtime.h>
 
 #include <cstring>
@@ -33,75 +35,70 @@ constexpr int kPgThreads = 256;
 
 struct PeerGatherArgs {
   const uint8_t* src;
-  int64_t rows, row_bytes, src_stride;  // bytes
+  int64_t rows, row_words, src_stride;  // row_words: 4-byte words per row; stride in bytes
   uint8_t* base[kPgMaxWorld];           // each rank's region as mapped here
   int world, rank;
-  int64_t data_off;                     // this call's buffer within a region
-  int64_t row_total;                    // world * row_bytes
-  int64_t flags_off;                    // flags array within a region
+  int64_t out_off;                      // this call's output buffer within a region
+  int64_t land_off;                     // this call's landing area within a region
   uint32_t* epoch;                      // this rank's local state
   uint32_t* counter;
   int* err;
 };
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_pair(uint32_t* p, uint32_t v, uint32_t flag) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(v), "r"(flag) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void fence_acq_rel_sys() {
-  asm volatile("fence.acq_rel.sys;" ::: "memory");
+__device__ __forceinline__ void ld_pair(const uint32_t* p, uint32_t& v, uint32_t& flag) {
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v), "=r"(flag) : "l"(p) : "memory");
 }
 
 __global__ void __launch_bounds__(kPgThreads) peer_gather_kernel(const PeerGatherArgs a) {
-  grid_dep_wait();  // the rows come from the previous kernel
-  const int64_t vpr = a.row_bytes / 16;
-  const int64_t total = a.rows * vpr;
-  for (int64_t i = blockIdx.x * (int64_t)kPgThreads + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * kPgThreads) {
-    const int64_t r = i / vpr, c = i - r * vpr;
-    const uint4 v = *reinterpret_cast<const uint4*>(a.src + r * a.src_stride + c * 16);
-    const int64_t off = a.data_off + r * a.row_total + a.rank * a.row_bytes + c * 16;
-    for (int p = 0; p < a.world; ++p) *reinterpret_cast<uint4*>(a.base[p] + off) = v;
+  grid_dep_wait();  // the rows come from the previous kernel; the last call has finished
+  const uint32_t e = *a.epoch + 1;  // this call's epoch (raised by the last CTA below)
+  const int64_t rw = a.row_words;
+  const int64_t nthreads = (int64_t)gridDim.x * kPgThreads;
+  const int64_t t0i = blockIdx.x * (int64_t)kPgThreads + threadIdx.x;
+  // ---- send: word w of row r -> landing slot (r, rank, w) of every rank
+  for (int64_t i = t0i; i < a.rows * rw; i += nthreads) {
+    const int64_t r = i / rw, w = i - r * rw;
+    const uint32_t v = *reinterpret_cast<const uint32_t*>(a.src + r * a.src_stride + w * 4);
+    const int64_t slot = (r * a.world + a.rank) * rw + w;
+    for (int p = 0; p < a.world; ++p)
+      st_pair(reinterpret_cast<uint32_t*>(a.base[p] + a.land_off) + 2 * slot, v, e);
   }
-  // One system-scope fence per CTA: the barrier orders the CTA's stores before it.
-  __syncthreads();
-  if (threadIdx.x != 0) return;
-  __threadfence_system();
-  if (gridDim.x > 1) {
-    if (atomicAdd(a.counter, 1u) != gridDim.x - 1) return;
-    // Last CTA: every CTA's stores were fenced before its arrival.
-    atomicExch(a.counter, 0u);
-    __threadfence_system();
-  }
-  // Publish this call to every rank, then wait for the same call of every rank.
-  const uint32_t e = *a.epoch + 1;
-  *a.epoch = e;
-  for (int p = 0; p < a.world; ++p)
-    st_release_sys(reinterpret_cast<uint32_t*>(a.base[p] + a.flags_off) + a.rank, e);
-  const uint32_t* mine = reinterpret_cast<const uint32_t*>(a.base[a.rank] + a.flags_off);
-  // After one wait has run out (a peer gone or stuck) later calls do not wait again:
-  // a persistent error word turns a broken rendezvous into one 2 s delay, not one
-  // per call.
-  if (a.err && (*reinterpret_cast<volatile int*>(a.err) & FI_DEVERR_TIMEOUT)) return;
+  // ---- receive: every rank's words of every row, unpacked to [row][rank][word]
+  uint32_t* land = reinterpret_cast<uint32_t*>(a.base[a.rank] + a.land_off);
+  uint32_t* out = reinterpret_cast<uint32_t*>(a.base[a.rank] + a.out_off);
+  // after one wait has run out (a peer gone or stuck) later calls do not wait again
+  bool give_up = a.err && (*reinterpret_cast<volatile int*>(a.err) & FI_DEVERR_TIMEOUT);
   const unsigned long long t0 = globaltimer_ns();
-  for (int p = 0; p < a.world; ++p) {
+  for (int64_t i = t0i; i < a.rows * a.world * rw; i += nthreads) {
+    uint32_t v, f;
+    ld_pair(land + 2 * i, v, f);
     uint32_t spins = 0;
-    while ((int32_t)(ld_relaxed_sys(mine + p) - e) < 0) {
+    while (f != e && !give_up) {
       if ((++spins & 63u) == 0u && globaltimer_ns() - t0 > kWaitTimeoutNs) {
         set_error(a.err, FI_DEVERR_TIMEOUT);
-        return;
+        give_up = true;
       }
+      ld_pair(land + 2 * i, v, f);
     }
+    out[i] = v;  // landing slot (r, p, w) and output word (r, p*rw + w) share the index
   }
-  fence_acq_rel_sys();  // the peers' rows are visible to this kernel's successors
+  // ---- the last CTA to finish raises the epoch for the next call
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(a.counter, 1u) == gridDim.x - 1) {
+    atomicExch(a.counter, 0u);
+    *a.epoch = e;
+  }
 }
 
-static int64_t pg_data_bytes(int64_t nbuf, int64_t max_rows, int64_t row_total) {
+// Output buffers, then the landing area (8 bytes per 4-byte word).
+static int64_t pg_out_bytes(int64_t nbuf, int64_t max_rows, int64_t row_total) {
   return (nbuf * max_rows * row_total + 255) / 256 * 256;
+}
+static int64_t pg_data_bytes(int64_t nbuf, int64_t max_rows, int64_t row_total) {
+  return pg_out_bytes(nbuf, max_rows, row_total) + 2 * pg_out_bytes(nbuf, max_rows, row_total);
 }
 
 }  // namespace fi
@@ -186,19 +183,21 @@ extern "C" int fi_peer_gather(const void* src, int64_t rows, int64_t row_bytes,
   }
   a.src = static_cast<const uint8_t*>(src);
   a.rows = rows;
-  a.row_bytes = row_bytes;
+  a.row_words = row_bytes / 4;
   a.src_stride = src_row_stride_bytes;
   a.world = (int)world;
   a.rank = (int)rank;
-  a.row_total = world * row_bytes;
-  a.data_off = buffer * max_rows * a.row_total;
-  a.flags_off = pg_data_bytes(nbuf, max_rows, a.row_total);
-  uint32_t* local = reinterpret_cast<uint32_t*>(a.base[rank] + a.flags_off) + kPgFlags;
+  const int64_t row_total = world * row_bytes;
+  a.out_off = buffer * max_rows * row_total;
+  a.land_off = pg_out_bytes(nbuf, max_rows, row_total) + 2 * buffer * max_rows * row_total;
+  uint32_t* local = reinterpret_cast<uint32_t*>(a.base[rank] +
+                                                pg_data_bytes(nbuf, max_rows, row_total)) +
+                    kPgFlags;
   a.epoch = local;
   a.counter = local + 1;
   a.err = error_flag;
-  const int64_t total = rows * (row_bytes / 16);
-  int64_t blocks = (total + kPgThreads * 8 - 1) / (kPgThreads * 8);  // ~8 vectors a thread
+  const int64_t total = rows * world * (row_bytes / 4);  // words received
+  int64_t blocks = (total + kPgThreads * 16 - 1) / (kPgThreads * 16);  // ~16 words a thread
   if (blocks < 1) blocks = 1;
   const int64_t cap = (int64_t)sm_count() * 4;
   if (blocks > cap) blocks = cap;
