@@ -89,6 +89,56 @@ def _worker(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
+def test_wait_runs_out_and_reports_timeout(cuda_device):
+    """One GPU, one kernel: rank 0 of a two-rank gather whose rank 1 never calls (both
+    regions are plain memory of this GPU; nothing writes rank 1's words). The wait
+    gives up after its 2 s bound, the host reads FI_DEVERR_TIMEOUT, rank 0's own rows
+    arrived, a second call with the same error word returns at once without waiting,
+    and the context still runs kernels (a one-rank gather gives its input back)."""
+    import ctypes
+    import time
+    from fast_infer_b200 import _lib
+    lib = _lib.load()
+    world, rows, elems, nbuf = 2, 4, 256, 2
+    row_bytes = elems * 2
+    nbytes = lib.fi_peer_gather_bytes(nbuf, rows, world * row_bytes)
+    regions = [torch.zeros(nbytes, dtype=torch.uint8, device=cuda_device) for _ in range(world)]
+    bases = (ctypes.c_void_p * world)(*[r.data_ptr() for r in regions])
+    err = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    x = torch.randn(rows, elems, device=cuda_device).half()
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+
+    def gather(b, bs, w, e):
+        st = lib.fi_peer_gather(x.data_ptr(), rows, row_bytes, row_bytes,
+                                ctypes.cast(bs, ctypes.POINTER(ctypes.c_void_p)), w, 0, b,
+                                nbuf, rows, e.data_ptr(), stream)
+        _lib.check(st, "peer gather")
+
+    torch.cuda.synchronize()
+    t0 = time.monotonic()
+    gather(0, bases, world, err)
+    torch.cuda.synchronize()
+    waited = time.monotonic() - t0
+    assert int(err.item()) == _lib.FI_DEVERR_TIMEOUT
+    assert 1.5 < waited < 30.0, waited
+    out = regions[0][:rows * world * row_bytes].view(torch.float16).view(rows, world * elems)
+    assert torch.equal(out[:, :elems], x)  # its own rows landed; rank 1's never came
+
+    t0 = time.monotonic()
+    gather(1, bases, world, err)  # the sticky error word: no second wait
+    torch.cuda.synchronize()
+    assert time.monotonic() - t0 < 1.0
+    assert int(err.item()) == _lib.FI_DEVERR_TIMEOUT
+
+    one = torch.zeros(lib.fi_peer_gather_bytes(nbuf, rows, row_bytes), dtype=torch.uint8,
+                      device=cuda_device)
+    err1 = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    gather(0, (ctypes.c_void_p * 1)(one.data_ptr()), 1, err1)
+    torch.cuda.synchronize()
+    assert int(err1.item()) == 0
+    assert torch.equal(one[:rows * row_bytes].view(torch.float16).view(rows, elems), x)
+
+
 def test_peer_gather_all_gpus(tmp_path):
     world = min(torch.cuda.device_count(), 8)
     if world < 2:
