@@ -23,6 +23,7 @@ FI_ERR_CUDA = 5
 FI_DEVERR_TIMEOUT = 1
 FI_DEVERR_BAD_BLOCK = 2
 FI_DEVERR_CONTEXT_LEN = 4
+FI_STATIC_WEIGHTS = 1
 
 _STATUS_NAMES = {
     FI_ERR_INVALID_ARG: "FI_ERR_INVALID_ARG",
@@ -68,13 +69,13 @@ SIGNATURES = {
     "fi_int4_quantize": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64p, _i64p, _i64p,
                                         _vp]),
     "fi_small_gemm": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _f32, _i64, _i64, _i64, _i64p,
-                                     _i64p, _i64p, _i64p, _vp, _vp]),
+                                     _i64p, _i64p, _i64p, _i64, _vp, _vp]),
     "fi_small_gemm_folded": (ctypes.c_int, [_vp, _vp, _vp, _vp, _f32, _i64, _i64, _i64, _i64p,
-                                            _i64p, _i64p, _i64p, _vp, _vp]),
+                                            _i64p, _i64p, _i64p, _i64, _vp, _vp]),
     "fi_qkv_rope_kv_write": (ctypes.c_int, [_vp, _vp, _f32, _i64, _i64, _i64, _i64, _i64, _i64p,
                                             _i64p, _vp, _vp, _i64, _i64, _vp, _vp, _i64p, _vp,
                                             _vp, _vp, _i64, _i64, _i64, _i64p, _i64p, _i64p,
-                                            _vp, _vp]),
+                                            _i64, _vp, _vp]),
     "fi_peer_gather_bytes": (_sz, [_i64, _i64, _i64]),
     "fi_peer_alloc": (ctypes.c_int, [_sz, ctypes.POINTER(_vp), _vp]),
     "fi_peer_open": (ctypes.c_int, [_vp, ctypes.POINTER(_vp)]),

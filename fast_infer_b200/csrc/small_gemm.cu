@@ -47,6 +47,7 @@ struct SgArgs {
   __half* c;
   int* err;
   int M, N, K, rounds, xstride;
+  int w_static;  // FI_STATIC_WEIGHTS: weight tiles may load before the dependency wait
   float eps;
   int64_t xs0, cs0, cs1, rs0, rs1;
 };
@@ -92,12 +93,22 @@ __global__ void __launch_bounds__(kSgThreads, 1)
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       prefetch_tmap(&tm_w);
-      for (int q = 0; q < total && q < kSgStages; ++q)  // weights only to L2 before the wait
-        tma_prefetch_l2_3d(&tm_w, 0, (blockIdx.x + (q / a.rounds) * gridDim.x) * kSgRows,
-                           (q % a.rounds) * kSgWarps);
+      // Constant weights (FI_STATIC_WEIGHTS): the first stages load while the previous
+      // kernel still runs; otherwise they only go to L2 before the wait.
+      const int pre = a.w_static ? (total < kSgStages ? total : kSgStages) : 0;
+      for (int q = 0; q < total && q < kSgStages; ++q) {
+        const int item = blockIdx.x + (q / a.rounds) * gridDim.x, r = q % a.rounds;
+        if (q < pre) {
+          mbar_arrive_expect_tx(&bars->full[q], kSgStageBytes);
+          tma_load_3d(stages + q * kSgStageBytes, &tm_w, &bars->full[q], 0, item * kSgRows,
+                      r * kSgWarps);
+        } else {
+          tma_prefetch_l2_3d(&tm_w, 0, item * kSgRows, r * kSgWarps);
+        }
+      }
       grid_dep_wait();
       bool dead = false;
-      for (int q = 0; q < total; ++q) {
+      for (int q = pre; q < total; ++q) {
         const int st = q % kSgStages;
         if (q >= kSgStages && !dead)
           dead = !mbar_wait(&bars->empty[st], ((q / kSgStages) - 1) & 1, a.err);
@@ -285,6 +296,7 @@ struct SsArgs {
   __half* c;
   int* err;
   int M, N, K, rounds;
+  int w_static;  // FI_STATIC_WEIGHTS: weight tiles may load before the dependency wait
   float eps;
   int64_t cs0, cs1, rs0, rs1;
   // kRope epilogue: RoPE of q / k and the KV-cache slot writes of k / v (one token per
@@ -340,7 +352,15 @@ __global__ void __launch_bounds__(kSgThreads, kSsStages == 2 ? 3 : 2)
     if (lane == 0) {
       prefetch_tmap(&tm_w);
       prefetch_tmap(&tm_x);
-      for (int q = 0; q < total && q < kSsStages; ++q)  // weights only to L2 before the wait
+      // Constant weights (FI_STATIC_WEIGHTS): the weight halves of the first stages
+      // load while the previous kernel still runs (x, its output, after the wait).
+      const int pre = a.w_static ? (total < kSsStages ? total : kSsStages) : 0;
+      for (int q = 0; q < pre; ++q) {
+        mbar_arrive_expect_tx(&bars->full[q], kSsStageBytes);
+        tma_load_3d(stages + q * kSsStageBytes, &tm_w, &bars->full[q], 0,
+                    (blockIdx.x + (q / a.rounds) * gridDim.x) * kSgRows, (q % a.rounds) * kSgWarps);
+      }
+      for (int q = pre; q < total && q < kSsStages; ++q)  // weights only to L2 before the wait
         tma_prefetch_l2_3d(&tm_w, 0, (blockIdx.x + (q / a.rounds) * gridDim.x) * kSgRows,
                            (q % a.rounds) * kSgWarps);
       grid_dep_wait();  // x is the previous kernel's output
@@ -351,8 +371,10 @@ __global__ void __launch_bounds__(kSgThreads, kSsStages == 2 ? 3 : 2)
           dead = !mbar_wait(&bars->empty[st], ((q / kSsStages) - 1) & 1, a.err);
         const int item = blockIdx.x + (q / a.rounds) * gridDim.x, r = q % a.rounds;
         uint8_t* sp = stages + st * kSsStageBytes;
-        mbar_arrive_expect_tx(&bars->full[st], kSsStageBytes);
-        tma_load_3d(sp, &tm_w, &bars->full[st], 0, item * kSgRows, r * kSgWarps);
+        if (q >= pre) {
+          mbar_arrive_expect_tx(&bars->full[st], kSsStageBytes);
+          tma_load_3d(sp, &tm_w, &bars->full[st], 0, item * kSgRows, r * kSgWarps);
+        }
         // x rows past M read as zeros (outside the tensor)
         tma_load_3d(sp + kSgStageBytes, &tm_x, &bars->full[st], 0, 0, r * kSgWarps);
       }
@@ -587,7 +609,7 @@ static int small_gemm_streamed(const void* x, const void* w, void* c, const void
                                bool fold, float eps, int64_t m, int64_t n, int64_t k,
                                const int64_t* x_strides, const int64_t* w_strides,
                                const int64_t* c_strides, const int64_t* residual_strides,
-                               int32_t* error_flag, cudaStream_t st) {
+                               int64_t flags, int32_t* error_flag, cudaStream_t st) {
   CUtensorMap tw, tx;
   {
     const int r = stream_maps(x, w, m, n, k, x_strides, w_strides, &tw, &tx);
@@ -602,6 +624,7 @@ static int small_gemm_streamed(const void* x, const void* w, void* c, const void
   a.N = (int)n;
   a.K = (int)k;
   a.rounds = (int)((k + kSgRoundK - 1) / kSgRoundK);
+  a.w_static = (flags & FI_STATIC_WEIGHTS) != 0;
   a.eps = eps;
   a.cs0 = c_strides[0];
   a.cs1 = c_strides[1];
@@ -622,10 +645,12 @@ extern "C" int fi_small_gemm(const void* x, const void* w, void* c, const void* 
                              const void* norm_weight, float eps, int64_t m, int64_t n, int64_t k,
                              const int64_t* x_strides, const int64_t* w_strides,
                              const int64_t* c_strides, const int64_t* residual_strides,
-                             int32_t* error_flag, void* stream) {
+                             int64_t flags, int32_t* error_flag, void* stream) {
   using namespace fi;
   clear_error();
   if (m < 0 || n < 0 || k <= 0) return fail(FI_ERR_INVALID_ARG, "fi_small_gemm: bad sizes");
+  if (flags & ~(int64_t)FI_STATIC_WEIGHTS)
+    return fail(FI_ERR_INVALID_ARG, "fi_small_gemm: unknown flags %lld", (long long)flags);
   if (m > kSgMaxM)
     return fail(FI_ERR_UNSUPPORTED, "fi_small_gemm: M (%lld) > %d; use a dense GEMM",
                 (long long)m, kSgMaxM);
@@ -641,7 +666,7 @@ extern "C" int fi_small_gemm(const void* x, const void* w, void* c, const void* 
                 "strides that are multiples of 8 elements");
   if (!norm_weight)  // x straight from global memory by TMA: the streamed variant
     return small_gemm_streamed(x, w, c, residual, false, eps, m, n, k, x_strides, w_strides,
-                               c_strides, residual_strides, error_flag,
+                               c_strides, residual_strides, flags, error_flag,
                                static_cast<cudaStream_t>(stream));
   CUtensorMap tm;
   {
@@ -664,6 +689,7 @@ extern "C" int fi_small_gemm(const void* x, const void* w, void* c, const void* 
   a.K = (int)k;
   a.rounds = (int)((k + kSgRoundK - 1) / kSgRoundK);
   a.xstride = a.rounds * kSgRoundK + 8;  // + 16 bytes: conflict-free ldmatrix rows
+  a.w_static = (flags & FI_STATIC_WEIGHTS) != 0;
   a.eps = eps;
   a.xs0 = x_strides[0];
   a.cs0 = c_strides[0];
@@ -685,11 +711,13 @@ extern "C" int fi_small_gemm_folded(const void* x, const void* w_folded, void* c
                                     const void* residual, float eps, int64_t m, int64_t n,
                                     int64_t k, const int64_t* x_strides,
                                     const int64_t* w_strides, const int64_t* c_strides,
-                                    const int64_t* residual_strides, int32_t* error_flag,
-                                    void* stream) {
+                                    const int64_t* residual_strides, int64_t flags,
+                                    int32_t* error_flag, void* stream) {
   using namespace fi;
   clear_error();
   if (m < 0 || n < 0 || k <= 0) return fail(FI_ERR_INVALID_ARG, "fi_small_gemm_folded: bad sizes");
+  if (flags & ~(int64_t)FI_STATIC_WEIGHTS)
+    return fail(FI_ERR_INVALID_ARG, "fi_small_gemm_folded: unknown flags %lld", (long long)flags);
   if (m > kSgMaxM)
     return fail(FI_ERR_UNSUPPORTED, "fi_small_gemm_folded: M (%lld) > %d", (long long)m, kSgMaxM);
   if (k % kSgChunk != 0 || k > (1 << 20) || n > (1 << 30))
@@ -705,7 +733,7 @@ extern "C" int fi_small_gemm_folded(const void* x, const void* w_folded, void* c
                 "fi_small_gemm_folded: x / w need 16-byte aligned bases, unit inner strides and "
                 "row strides that are multiples of 8 elements");
   return small_gemm_streamed(x, w_folded, c, residual, true, eps, m, n, k, x_strides, w_strides,
-                             c_strides, residual_strides, error_flag,
+                             c_strides, residual_strides, flags, error_flag,
                              static_cast<cudaStream_t>(stream));
 }
 
@@ -716,12 +744,14 @@ extern "C" int fi_qkv_rope_kv_write(
     const int32_t* start_pos, void* q_out, const int64_t* q_out_strides, void* k_cache,
     void* v_cache, const int32_t* block_table, int64_t num_blocks, int64_t block_size,
     int64_t max_blocks_per_seq, const int64_t* kc_strides, const int64_t* vc_strides,
-    const int64_t* bt_strides, int32_t* error_flag, void* stream) {
+    const int64_t* bt_strides, int64_t flags, int32_t* error_flag, void* stream) {
   using namespace fi;
   clear_error();
   if (batch < 0 || k <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || block_size <= 0 ||
       num_blocks <= 0 || max_blocks_per_seq <= 0 || table_rows <= 0)
     return fail(FI_ERR_INVALID_ARG, "fi_qkv_rope_kv_write: bad sizes");
+  if (flags & ~(int64_t)FI_STATIC_WEIGHTS)
+    return fail(FI_ERR_INVALID_ARG, "fi_qkv_rope_kv_write: unknown flags %lld", (long long)flags);
   if (head_dim != 128)
     return fail(FI_ERR_UNSUPPORTED, "fi_qkv_rope_kv_write: head_dim %lld != 128",
                 (long long)head_dim);
@@ -753,6 +783,7 @@ extern "C" int fi_qkv_rope_kv_write(
   a.N = (int)n;
   a.K = (int)k;
   a.rounds = (int)((k + kSgRoundK - 1) / kSgRoundK);
+  a.w_static = (flags & FI_STATIC_WEIGHTS) != 0;
   a.eps = eps;
   a.cos_tab = cos_table;
   a.sin_tab = sin_table;

@@ -175,7 +175,7 @@ STREAM_GEMM_MAX_M = 16
 
 def fp16_linear(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor = None,
                 norm_weight: torch.Tensor = None, eps: float = 1e-5,
-                out: torch.Tensor = None) -> torch.Tensor:
+                out: torch.Tensor = None, static_weight: bool = False) -> torch.Tensor:
     """``residual + rms_norm(x, norm_weight, eps) @ w.T`` in fp16 (fp32 accumulation).
 
     x [..., K], w [N, K] fp16 (the reference's linear layout, kernels/matmul.py:187-212);
@@ -183,7 +183,9 @@ def fp16_linear(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor = None,
     take one ``fi_small_gemm`` launch (norm on load, residual in the epilogue, a single
     rounding) up to ``SMALL_GEMM_MAX_M`` rows; more rows use ``rms_norm`` and the dense
     library GEMM with the residual as its beta = 1 input. ``out`` (may be
-    ``residual``) receives the result.
+    ``residual``) receives the result. ``static_weight``: ``w`` is constant (model
+    weights, not written by kernels still running), so the kernel's first weight tiles
+    load while the previous kernel finishes (``FI_STATIC_WEIGHTS``; same result bits).
     """
     if not x.is_cuda or not w.is_cuda:
         raise ValueError("x and w must be CUDA tensors (fast_infer_b200 has no CPU path)")
@@ -206,8 +208,9 @@ def fp16_linear(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor = None,
     if M <= limit and K % 64 == 0 and M > 0 and N > 0:
         if x2.stride(1) != 1 or x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
             x2 = x2.contiguous()
+        flags = _lib.FI_STATIC_WEIGHTS if static_weight else 0
         if w.stride(1) != 1 or w.stride(0) % 8 != 0 or w.data_ptr() % 16 != 0:
-            w = w.contiguous()
+            w, flags = w.contiguous(), 0  # a fresh copy is the previous kernel's output
         nw = norm_weight
         if nw is not None and (not nw.is_contiguous() or nw.data_ptr() % 16 != 0):
             nw = nw.contiguous()
@@ -220,7 +223,7 @@ def fp16_linear(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor = None,
                 nw.data_ptr() if nw is not None else None, float(eps), M, N, K,
                 _lib.strides(*x2.stride()), _lib.strides(*w.stride()),
                 _lib.strides(*o2.stride()),
-                _lib.strides(*r2.stride()) if r2 is not None else None,
+                _lib.strides(*r2.stride()) if r2 is not None else None, flags,
                 err.data_ptr() if err is not None else None, stream_of(x.device))
             _lib.check(st, "fp16_linear")
             device_errors(err, "fp16_linear")
@@ -241,13 +244,14 @@ def fold_rms_weight(w: torch.Tensor, norm_weight: torch.Tensor) -> torch.Tensor:
 
 
 def fp16_linear_folded(x: torch.Tensor, w_folded: torch.Tensor, eps: float = 1e-5,
-                       residual: torch.Tensor = None, out: torch.Tensor = None) -> torch.Tensor:
+                       residual: torch.Tensor = None, out: torch.Tensor = None,
+                       static_weight: bool = False) -> torch.Tensor:
     """``residual + rsqrt(mean(x^2) + eps) * (x @ w_folded.T)`` = rms_norm(x) @ w.T with
     the norm weight folded into ``w_folded`` (``fold_rms_weight``). Up to 16 rows: one
     ``fi_small_gemm_folded`` launch (x streamed with the weight tiles, the per-row
     factor applied in the epilogue); the rounding differs from the reference's
     normalised-then-rounded x by fp16 noise. More rows: the same formula with library
-    ops."""
+    ops. ``static_weight`` as in ``fp16_linear``."""
     if not x.is_cuda or not w_folded.is_cuda:
         raise ValueError("x and w must be CUDA tensors (fast_infer_b200 has no CPU path)")
     if x.dtype != torch.float16 or w_folded.dtype != torch.float16:
@@ -267,8 +271,9 @@ def fp16_linear_folded(x: torch.Tensor, w_folded: torch.Tensor, eps: float = 1e-
         if x2.stride(1) != 1 or x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
             x2 = x2.contiguous()
         w = w_folded
+        flags = _lib.FI_STATIC_WEIGHTS if static_weight else 0
         if w.stride(1) != 1 or w.stride(0) % 8 != 0 or w.data_ptr() % 16 != 0:
-            w = w.contiguous()
+            w, flags = w.contiguous(), 0  # a fresh copy is the previous kernel's output
         lib = _lib.load()
         with with_device(x.device):
             err = error_word(x.device)
@@ -277,7 +282,7 @@ def fp16_linear_folded(x: torch.Tensor, w_folded: torch.Tensor, eps: float = 1e-
                 r2.data_ptr() if r2 is not None else None, float(eps), M, N, K,
                 _lib.strides(*x2.stride()), _lib.strides(*w.stride()),
                 _lib.strides(*o2.stride()),
-                _lib.strides(*r2.stride()) if r2 is not None else None,
+                _lib.strides(*r2.stride()) if r2 is not None else None, flags,
                 err.data_ptr() if err is not None else None, stream_of(x.device))
             _lib.check(st, "fp16_linear_folded")
             device_errors(err, "fp16_linear_folded")

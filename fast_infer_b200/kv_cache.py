@@ -317,14 +317,15 @@ def permute_rope_rows(w: torch.Tensor, head_dim: int = 128) -> torch.Tensor:
 def qkv_rope_store(cache: KVCache, layer_idx: int, x: torch.Tensor, w_rope: torch.Tensor,
                    num_q_heads: int, cos_table: torch.Tensor, sin_table: torch.Tensor,
                    start_pos: torch.Tensor, eps: float = 1e-5,
-                   q_out: torch.Tensor = None) -> torch.Tensor:
+                   q_out: torch.Tensor = None, static_weight: bool = False) -> torch.Tensor:
     """Decode step, one launch: RMSNorm + QKV projection + RoPE + KV slot writes.
 
     x: [B, 1, K] or [B, K] fp16 (one new token per sequence, B <= 16); w_rope: the
     folded QKV weight (``kernels.matmul.fold_rms_weight``) with rows permuted by
     ``permute_rope_rows``; start_pos: [B] int32 device positions. The same bits as
     ``fp16_linear_folded`` followed by ``rope_and_store``. Returns rotated q
-    [B, 1, nq, D] (``q_out`` if given).
+    [B, 1, nq, D] (``q_out`` if given). ``static_weight``: ``w_rope`` is constant, so
+    its first tiles load while the previous kernel finishes (``FI_STATIC_WEIGHTS``).
     """
     cache.sync_block_table()
     D, nkv = cache.head_dim, cache.num_heads
@@ -356,6 +357,7 @@ def qkv_rope_store(cache: KVCache, layer_idx: int, x: torch.Tensor, w_rope: torc
             kc.data_ptr(), vc.data_ptr(), cache.block_table.data_ptr(), cache.num_blocks,
             cache.block_size, cache.max_blocks_per_seq, _lib.strides(*kc.stride()),
             _lib.strides(*vc.stride()), _lib.strides(*cache.block_table.stride()),
+            _lib.FI_STATIC_WEIGHTS if static_weight else 0,
             err.data_ptr() if err is not None else None, stream_of(cache.device))
         _lib.check(st, "qkv_rope_store")
         device_errors(err, "qkv_rope_store")

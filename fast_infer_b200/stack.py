@@ -189,14 +189,15 @@ class AttentionStack:
         span = self.cache.max_blocks_per_seq * 64
         h = self._h_in.clone()  # the residual stream is updated in place below
         for li, w in enumerate(self.layers):
-            # RMSNorm + QKV projection + RoPE + KV slot writes in one launch
+            # RMSNorm + QKV projection + RoPE + KV slot writes in one launch; the
+            # weights are constant, so their first tiles load during the previous kernel
             q = qkv_rope_store(self.cache, li, h, w["wqkv_rope"], nq, self.cos, self.sin,
-                               self._dev_start, eps=self.eps)
+                               self._dev_start, eps=self.eps, static_weight=True)
             o = paged_attention(q[:, 0], self.cache.k[li], self.cache.v[li],
                                 self.cache.block_table, 64, 0, context_lens=self._dev_ctx,
                                 max_context_len=span, workspace=self._ws)
             o = self._gather(o.reshape(B, 1, nq * D), li)
-            fp16_linear(o, w["wo_t"], residual=h, out=h)  # h += o @ Wo, one launch
+            fp16_linear(o, w["wo_t"], residual=h, out=h, static_weight=True)  # h += o @ Wo
         self._dev_ctx.add_(1)
         self._dev_start.add_(1)
         self._h_in.copy_(h)

@@ -44,6 +44,14 @@ extern "C" {
 #define FI_DEVERR_CONTEXT_LEN 4 /* a context length beyond max_context_len or the block table;
                                   that sequence was truncated */
 
+/* ---- call flags (the `flags` argument of the decode GEMMs) -------------- */
+/* The weight operand is constant: no kernel that may still be running when the call
+ * is made writes it. The call's first weight tiles then load while the previous
+ * kernel on the stream finishes (programmatic dependent launch), instead of after
+ * it. Results are the same bits either way; without the flag the weights are read
+ * only after the dependency wait, so they may be the previous kernel's output. */
+#define FI_STATIC_WEIGHTS 1
+
 /* Library version (major*10000 + minor*100 + patch). */
 int fi_version(void);
 
@@ -283,7 +291,7 @@ int fi_int4_quantize(const void* w, void* packed, void* scales, int64_t n, int64
  * 8 elements, 16-byte aligned bases); fp32 accumulation, one fp16 rounding at the
  * end. norm_weight [k] (NULL: no norm) applies fi_rms_norm's arithmetic with eps;
  * residual NULL: no add (it may alias c). k a multiple of 64; m > 16 returns
- * FI_ERR_UNSUPPORTED (use a dense GEMM).
+ * FI_ERR_UNSUPPORTED (use a dense GEMM). flags: 0 or FI_STATIC_WEIGHTS.
  *
  * Replaces, at decode batch sizes: kernels/rms_norm.py:29-43 followed by
  * kernels/matmul.py:187-212 `_fp16_matmul` (the QKV projection of model.py:82-93),
@@ -292,7 +300,8 @@ int fi_int4_quantize(const void* w, void* packed, void* scales, int64_t n, int64
 int fi_small_gemm(const void* x, const void* w, void* c, const void* residual,
                   const void* norm_weight, float eps, int64_t m, int64_t n, int64_t k,
                   const int64_t* x_strides, const int64_t* w_strides, const int64_t* c_strides,
-                  const int64_t* residual_strides, int32_t* error_flag, void* stream);
+                  const int64_t* residual_strides, int64_t flags, int32_t* error_flag,
+                  void* stream);
 
 /*
  * The same with the RMSNorm weight folded into the weights: w_folded[n, j] =
@@ -306,7 +315,8 @@ int fi_small_gemm(const void* x, const void* w, void* c, const void* residual,
 int fi_small_gemm_folded(const void* x, const void* w_folded, void* c, const void* residual,
                          float eps, int64_t m, int64_t n, int64_t k, const int64_t* x_strides,
                          const int64_t* w_strides, const int64_t* c_strides,
-                         const int64_t* residual_strides, int32_t* error_flag, void* stream);
+                         const int64_t* residual_strides, int64_t flags, int32_t* error_flag,
+                         void* stream);
 
 /*
  * Decode-step QKV projection with RMSNorm, RoPE and the KV-cache slot writes in one
@@ -320,7 +330,7 @@ int fi_small_gemm_folded(const void* x, const void* w_folded, void* c, const voi
  * its rows permuted per head: for head h and c in 0..7, rows 128h + 16c .. +7 hold
  * dims 8c .. 8c+7 and rows 128h + 16c + 8 .. +15 hold dims 64 + 8c .. (so each
  * 16-row tile carries its rotary pairs). head_dim 128; cos/sin fp32 [table_rows,
- * table_stride].
+ * table_stride]. flags: 0 or FI_STATIC_WEIGHTS (for w_rope).
  *
  * Replaces, at decode batch sizes: the RMSNorm + QKV projection (model.py:82-93) and
  * the RoPE + slot writes (kernels/rope.py:26-44, model.py:101,185-201).
@@ -333,7 +343,7 @@ int fi_qkv_rope_kv_write(const void* x, const void* w_rope, float eps, int64_t b
                          const int64_t* q_out_strides, void* k_cache, void* v_cache,
                          const int32_t* block_table, int64_t num_blocks, int64_t block_size,
                          int64_t max_blocks_per_seq, const int64_t* kc_strides,
-                         const int64_t* vc_strides, const int64_t* bt_strides,
+                         const int64_t* vc_strides, const int64_t* bt_strides, int64_t flags,
                          int32_t* error_flag, void* stream);
 
 /*

@@ -138,16 +138,28 @@ def test_small_gemm_validation():
     from fast_infer_b200 import _lib
     lib = _lib.load()
     s2 = _lib.strides(1, 1)
+    s3 = _lib.strides(1, 1, 1)
+    s4 = _lib.strides(1, 1, 1, 1)
     # more than 16 rows, K not a multiple of 64, null pointers: rejected on the host
     assert lib.fi_small_gemm(None, None, None, None, None, 1e-5, 17, 8, 64, s2, s2, s2, None,
-                             None, None) == _lib.FI_ERR_UNSUPPORTED
+                             0, None, None) == _lib.FI_ERR_UNSUPPORTED
     assert lib.fi_small_gemm(None, None, None, None, None, 1e-5, 4, 8, 100, s2, s2, s2, None,
-                             None, None) == _lib.FI_ERR_UNSUPPORTED
+                             0, None, None) == _lib.FI_ERR_UNSUPPORTED
     assert lib.fi_small_gemm(None, None, None, None, None, 1e-5, 4, 8, 64, s2, s2, s2, None,
-                             None, None) == _lib.FI_ERR_INVALID_ARG
+                             0, None, None) == _lib.FI_ERR_INVALID_ARG
     assert lib.fi_small_gemm(None, None, None, None, None, 1e-5, 0, 8, 64, s2, s2, s2, None,
-                             None, None) == _lib.FI_OK
+                             0, None, None) == _lib.FI_OK
     assert lib.fi_small_gemm_folded(None, None, None, None, 1e-5, 17, 8, 64, s2, s2, s2, None,
-                                    None, None) == _lib.FI_ERR_UNSUPPORTED
+                                    0, None, None) == _lib.FI_ERR_UNSUPPORTED
     assert lib.fi_small_gemm_folded(None, None, None, None, 1e-5, 4, 8, 64, s2, s2, s2, None,
-                                    None, None) == _lib.FI_ERR_INVALID_ARG
+                                    _lib.FI_STATIC_WEIGHTS, None, None) == _lib.FI_ERR_INVALID_ARG
+    # flags: FI_STATIC_WEIGHTS is the only bit; any other is rejected before anything else
+    for flags in (2, 1 << 40, -1):
+        assert lib.fi_small_gemm(None, None, None, None, None, 1e-5, 0, 8, 64, s2, s2, s2,
+                                 None, flags, None, None) == _lib.FI_ERR_INVALID_ARG
+        assert lib.fi_small_gemm_folded(None, None, None, None, 1e-5, 4, 8, 64, s2, s2, s2,
+                                        None, flags, None, None) == _lib.FI_ERR_INVALID_ARG
+        assert lib.fi_qkv_rope_kv_write(None, None, 1e-5, 4, 64, 3, 1, 128, s2, s2, None, None,
+                                        16, 128, None, None, s3, None, None, None, 8, 64, 2,
+                                        s4, s4, s2, flags, None, None) == _lib.FI_ERR_INVALID_ARG
+    assert "unknown flags" in lib.fi_last_error().decode()

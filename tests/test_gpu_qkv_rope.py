@@ -2,7 +2,8 @@
 launch (fi_qkv_rope_kv_write via kv_cache.qkv_rope_store): the same bits as the two
 launches it replaces — the folded-norm projection (fp16_linear_folded) followed by
 rope_and_store — for the rotated q and for every K/V page of the pool, at ragged
-positions that cross page boundaries, 1 to 16 sequences, 24/8 and 12/4 heads."""
+positions that cross page boundaries, 1 to 16 sequences, 24/8 and 12/4 heads; with
+FI_STATIC_WEIGHTS too."""
 
 import pytest
 import torch
@@ -49,6 +50,11 @@ def test_fused_equals_projection_then_rope_store(cuda_device, batch, nq, nkv):
     torch.cuda.synchronize()
     assert qb.shape == qa.shape
     assert torch.equal(qa, qb)
+    assert torch.equal(ca.k, cb.k) and torch.equal(ca.v, cb.v)
+    # constant weights (first tiles loaded before the dependency wait): the same bits
+    qs = qkv_rope_store(cb, 1, x, wr, nq, cos, sin, pos, eps=1e-5, static_weight=True)
+    torch.cuda.synchronize()
+    assert torch.equal(qs, qa)
     assert torch.equal(ca.k, cb.k) and torch.equal(ca.v, cb.v)
     # the new token really landed: row pos % 64 of page block_table[b, pos // 64]
     bt = ca.block_table.cpu()

@@ -101,3 +101,50 @@ def test_folded_norm(cuda_device, m, n, k):
     h = res.clone()
     fp16_linear_folded(x, wf, residual=h, out=h)
     assert torch.equal(h, fp16_linear_folded(x, wf, residual=res))
+
+
+@pytest.mark.parametrize("m", [1, 8, 16])
+def test_static_weights_same_bits(cuda_device, m):
+    """FI_STATIC_WEIGHTS (weight tiles loaded before the dependency wait) changes no
+    bit: staged (norm) and streamed paths, folded, and a back-to-back chain in which
+    every x is the previous kernel's output, eagerly and from a CUDA graph."""
+    from fast_infer_b200.kernels.matmul import fold_rms_weight, fp16_linear, fp16_linear_folded
+    x, w, res, nw = _data(m, 3072, 3072, cuda_device, 40 + m)
+    for kw in ({}, {"norm_weight": nw}, {"residual": res}):
+        assert torch.equal(fp16_linear(x, w, static_weight=True, **kw), fp16_linear(x, w, **kw))
+    wf = fold_rms_weight(w, nw)
+    assert torch.equal(fp16_linear_folded(x, wf, residual=res, static_weight=True),
+                       fp16_linear_folded(x, wf, residual=res))
+
+    g = torch.Generator(device=cuda_device)
+    g.manual_seed(3)
+    ws = [(torch.randn(3072, 3072, device=cuda_device, generator=g) * 0.02).half()
+          for _ in range(4)]
+
+    def chain(static, sync):
+        h = x
+        for i, wi in enumerate(ws):
+            h = (fp16_linear_folded(h, wi, static_weight=static) if i % 2 else
+                 fp16_linear(h, wi, residual=h, static_weight=static))
+            if sync:
+                torch.cuda.synchronize()
+        return h
+
+    ref = chain(False, True)
+    for _ in range(3):
+        out = chain(True, False)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    side = torch.cuda.Stream(cuda_device)
+    side.wait_stream(torch.cuda.current_stream(cuda_device))
+    with torch.cuda.stream(side):
+        chain(True, False)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            gout = chain(True, False)
+    torch.cuda.current_stream(cuda_device).wait_stream(side)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(gout, ref)
+    del graph
