@@ -2,7 +2,8 @@
 launch (fi_qkv_rope_kv_write via kv_cache.qkv_rope_store): the same bits as the two
 launches it replaces — the folded-norm projection (fp16_linear_folded) followed by
 rope_and_store — for the rotated q and for every K/V page of the pool, at ragged
-positions that cross page boundaries, 1 to 16 sequences, 24/8 and 12/4 heads; with
+positions that cross page boundaries, 1 to 16 sequences, 24/8 heads and the per-rank
+head counts of a stack sharded over 2, 4 and 8 GPUs (12/4, 6/2, 3/1); with
 FI_STATIC_WEIGHTS too."""
 
 import pytest
@@ -39,7 +40,8 @@ def _setup(dev, batch, nq, nkv, seed):
     return x, wf, permute_rope_rows(wf), cos, sin, pos, caches
 
 
-@pytest.mark.parametrize("batch,nq,nkv", [(1, 24, 8), (5, 24, 8), (16, 24, 8), (16, 12, 4)])
+@pytest.mark.parametrize("batch,nq,nkv", [(1, 24, 8), (5, 24, 8), (16, 24, 8), (16, 12, 4),
+                                            (16, 6, 2), (16, 3, 1), (7, 3, 1)])
 def test_fused_equals_projection_then_rope_store(cuda_device, batch, nq, nkv):
     from fast_infer_b200.kernels.matmul import fp16_linear_folded
     from fast_infer_b200.kv_cache import qkv_rope_store, rope_and_store
