@@ -77,6 +77,35 @@ def test_decode_validation_and_workspace_size():
     assert st == _lib.FI_ERR_WORKSPACE
 
 
+def test_automatic_split_rule():
+    """The automatic split-KV choice, read back through the workspace it needs: about
+    SMs / (2 x sequences x KV heads) splits per sequence, 4 to 32 pages each, and 32
+    pages per split once that is one split (148 SMs: a B200, and the count the library
+    assumes with no device)."""
+    import torch
+    if torch.cuda.is_available() and \
+            torch.cuda.get_device_properties(0).multi_processor_count != 148:
+        pytest.skip("rule values below are for 148 SMs")
+    lib = _lib.load()
+
+    def expect(batch, hq, hkv, max_ctx, sms=148):
+        pages = -(-max_ctx // 64)
+        splits = sms // (2 * batch * hkv)
+        pps = 32 if splits <= 1 else min(32, max(4, -(-pages // splits)))
+        n = -(-pages // pps)
+        return 0 if n <= 1 else batch * hq * n * (128 * 4 + 8)
+
+    cases = [(64, 24, 8, 4096, 2),     # config 3: 32 pages per split, two splits at most
+             (16, 24, 8, 1280, 1),     # the stack's decode step: unsplit
+             (256, 24, 8, 4096, 2),    # config 5
+             (1, 24, 8, 8192, 9),      # one long sequence: 9 splits of 15 pages
+             (2, 3, 1, 4096, 16)]      # one KV head: splits floored at 4 pages
+    for batch, hq, hkv, ctx, nsplit in cases:
+        ws = lib.fi_paged_decode_workspace_size(batch, hq, hkv, 128, ctx, 64, 0)
+        assert ws == expect(batch, hq, hkv, ctx), (batch, hq, hkv, ctx)
+        assert ws == (0 if nsplit == 1 else batch * hq * nsplit * (128 * 4 + 8))
+
+
 def test_kv_write_validation():
     lib = _lib.load()
     s4, s2 = _lib.strides(1, 1, 1, 1), _lib.strides(1, 1)
