@@ -31,6 +31,43 @@ def test_library_exports_every_declared_symbol():
     assert lib.fi_version() >= 100
 
 
+def _declarations():
+    """name -> parameter list (C text) of every function declared in include/*.h."""
+    out = {}
+    for h in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        for name, params in re.findall(r"\b(fi_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text):
+            params = " ".join(params.split())
+            out[name] = [] if params in ("", "void") else [x.strip() for x in params.split(",")]
+    return out
+
+
+def test_ctypes_signatures_match_the_header():
+    """Every binding in _lib.SIGNATURES has the header's argument count and, per
+    argument, a matching kind (pointer / int64 / int / size_t / float), and the
+    FI_* constants the Python layer mirrors equal the header's."""
+    decls = _declarations()
+    assert set(decls) == set(_lib.SIGNATURES)
+    scalar = {"int64_t": ctypes.c_int64, "int": ctypes.c_int, "size_t": ctypes.c_size_t,
+              "float": ctypes.c_float, "double": ctypes.c_double}
+    for name, params in decls.items():
+        argtypes = _lib.SIGNATURES[name][1]
+        assert len(argtypes) == len(params), (name, len(argtypes), len(params))
+        for i, (c, py) in enumerate(zip(params, argtypes)):
+            if "*" in c:
+                assert py in (ctypes.c_void_p, ctypes.c_char_p) or \
+                    issubclass(py, ctypes._Pointer), (name, i, c, py)
+            else:
+                ctype = c.replace("const ", "").rsplit(" ", 1)[0].strip()
+                assert scalar[ctype] is py, (name, i, c, py)
+    text = "".join(h.read_text() for h in (ROOT / "include").glob("*.h"))
+    defines = dict(re.findall(r"#define\s+(FI_[A-Z0-9_]+)\s+(-?\d+)\b", text))
+    mirrored = [n for n in dir(_lib) if re.fullmatch(r"FI_[A-Z0-9_]+", n) and n in defines]
+    assert {"FI_OK", "FI_ERR_WORKSPACE", "FI_DEVERR_TIMEOUT", "FI_STATIC_WEIGHTS"} <= set(mirrored)
+    for n in mirrored:
+        assert getattr(_lib, n) == int(defines[n]), n
+
+
 def _nul():
     return ctypes.c_void_p(0)
 
