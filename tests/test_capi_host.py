@@ -229,3 +229,44 @@ def test_small_gemm_validation():
                                         16, 128, None, None, s3, None, None, None, 8, 64, 2,
                                         s4, s4, s2, flags, None, None) == _lib.FI_ERR_INVALID_ARG
     assert "unknown flags" in lib.fi_last_error().decode()
+
+
+def test_peer_gather_host_checks():
+    """Peer gather set-up and call checks that answer before any device work: the
+    region size (this rank's output buffers plus an 8-byte landing slot per 4-byte
+    word of every buffer, plus a small local state), and the argument checks of
+    fi_peer_gather / fi_peer_alloc / fi_peer_open (null handles close and free as
+    no-ops)."""
+    lib = _lib.load()
+    assert lib.fi_peer_gather_bytes(0, 16, 1536) == 0
+    assert lib.fi_peer_gather_bytes(3, 0, 1536) == 0
+    assert lib.fi_peer_gather_bytes(3, 16, -1) == 0
+    for nbuf, rows, row_total in ((3, 16, 2 * 768), (28, 16, 8 * 768), (1, 1, 16)):
+        n = lib.fi_peer_gather_bytes(nbuf, rows, row_total)
+        data = nbuf * rows * row_total
+        assert 3 * data <= n <= 3 * data + 3 * 255 + 1024, (nbuf, rows, row_total, n)
+
+    bases = (ctypes.c_void_p * 2)(None, None)
+    pbases = ctypes.cast(bases, ctypes.POINTER(ctypes.c_void_p))
+
+    def gather(src=None, rows=4, row_bytes=256, stride=256, world=2, rank=0, buffer=0, nbuf=2,
+               max_rows=16, b=pbases):
+        return lib.fi_peer_gather(src, rows, row_bytes, stride, b, world, rank, buffer, nbuf,
+                                  max_rows, None, None)
+    bad = _lib.FI_ERR_INVALID_ARG
+    assert gather(world=0) == bad and gather(world=9) == bad
+    assert gather(rank=2) == bad and gather(rank=-1) == bad
+    assert gather(rows=17) == bad and gather(buffer=2) == bad and gather(nbuf=0) == bad
+    assert gather(row_bytes=24) == _lib.FI_ERR_ALIGNMENT
+    assert gather(stride=264) == _lib.FI_ERR_ALIGNMENT
+    assert gather() == bad                      # null source rows
+    assert gather(b=None) == bad                # no region table
+    assert "fi_peer_gather" in lib.fi_last_error().decode()
+
+    handle = ctypes.create_string_buffer(64)
+    out = ctypes.c_void_p()
+    assert lib.fi_peer_alloc(0, ctypes.byref(out), handle) == bad
+    assert lib.fi_peer_alloc(1024, None, handle) == bad
+    assert lib.fi_peer_open(None, ctypes.byref(out)) == bad
+    assert lib.fi_peer_close(None) == _lib.FI_OK
+    assert lib.fi_peer_free(None) == _lib.FI_OK
