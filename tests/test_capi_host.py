@@ -270,3 +270,36 @@ def test_peer_gather_host_checks():
     assert lib.fi_peer_open(None, ctypes.byref(out)) == bad
     assert lib.fi_peer_close(None) == _lib.FI_OK
     assert lib.fi_peer_free(None) == _lib.FI_OK
+
+
+def test_norm_rope_varlen_host_checks():
+    """fi_rms_norm, fi_rope_kv_write and fi_prefill_fwd_varlen reject bad sizes,
+    unsupported shapes and null pointers before any device work, and treat empty
+    inputs as no-ops."""
+    lib = _lib.load()
+    bad, unsup, ok = _lib.FI_ERR_INVALID_ARG, _lib.FI_ERR_UNSUPPORTED, _lib.FI_OK
+    # rms_norm(x, weight, out, rows, hidden, x_row_stride, out_row_stride, eps, stream)
+    assert lib.fi_rms_norm(None, None, None, -1, 3072, 3072, 3072, 1e-5, None) == bad
+    assert lib.fi_rms_norm(None, None, None, 4, 3070, 3072, 3072, 1e-5, None) == unsup
+    assert lib.fi_rms_norm(None, None, None, 0, 3072, 3072, 3072, 1e-5, None) == ok
+    assert lib.fi_rms_norm(None, None, None, 4, 3072, 3072, 3072, 1e-5, None) == bad
+
+    s2, s3, s4 = _lib.strides(1, 1), _lib.strides(1, 1, 1), _lib.strides(1, 1, 1, 1)
+
+    def rope(batch=2, seq=3, nq=24, nkv=8, d=128, ptr=None):
+        return lib.fi_rope_kv_write(ptr, batch, seq, nq, nkv, d, s4, ptr, ptr, 64, 128, None, 0,
+                                    ptr, s4, None, None, ptr, ptr, ptr, 8, 64, 4, s4, s4, s2,
+                                    None, None)
+    assert rope(batch=-1) == bad and rope(nkv=0) == bad
+    assert rope(d=100) == unsup
+    assert rope(batch=0) == ok and rope(seq=0) == ok
+    assert rope() == bad  # null pointers
+
+    def varlen(batch=2, hq=24, hkv=8, max_s=128, total=200, d=128):
+        return lib.fi_prefill_fwd_varlen(None, None, None, None, None, batch, hq, hkv, max_s,
+                                         total, d, s3, s3, s3, s3, 0.1, None, None)
+    assert varlen(batch=-1) == bad and varlen(hkv=0) == bad
+    assert varlen(d=64) == unsup
+    assert varlen(hq=24, hkv=7) == bad
+    assert varlen(batch=0) == ok and varlen(total=0) == ok
+    assert varlen() == bad  # null pointers
