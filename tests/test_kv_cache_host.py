@@ -57,3 +57,25 @@ def test_alloc_errors_reset_and_grow():
     with pytest.raises(RuntimeError, match="table full"):
         cache2.alloc_block(0)
     assert cache2.allocated_tokens() == 128
+
+
+def test_permute_rope_rows_layout():
+    """permute_rope_rows (the fused decode QKV weight layout): within each 128-row head,
+    16-row tile c holds dims 8c..8c+7 then 64+8c..64+8c+7, so each tile carries its
+    rotary pairs (d, d + 64); whole heads only; a pure row permutation."""
+    from fast_infer_b200.kv_cache import permute_rope_rows
+    heads, k = 5, 64
+    w = torch.arange(heads * 128, dtype=torch.float32)[:, None].repeat(1, k).half()
+    p = permute_rope_rows(w)
+    src = p[:, 0].float().long()
+    for h in range(heads):
+        for c in range(8):
+            for r in range(8):
+                assert src[128 * h + 16 * c + r] == 128 * h + 8 * c + r
+                assert src[128 * h + 16 * c + 8 + r] == 128 * h + 64 + 8 * c + r
+    assert sorted(src.tolist()) == list(range(heads * 128))
+    assert p.is_contiguous() and torch.equal(p[:, 1:], p[:, :1].expand(-1, k - 1))
+    with pytest.raises(ValueError):
+        permute_rope_rows(w[:100])
+    with pytest.raises(ValueError):
+        permute_rope_rows(w, head_dim=64)
