@@ -6,7 +6,6 @@ Public surface (same names and semantics as the reference modules they replace):
   (reference kernels/attention.py)
 * ``fast_infer_b200.kv_cache.KVCache`` plus ``store_kv_prefill`` / ``store_kv_decode``
   (reference kv_cache.py and model.py:162-201)
-* ``fast_infer_b200.config.LlamaConfig`` (reference config.py)
 * ``fast_infer_b200.shard`` — KV-head / sequence partitioning across GPUs.
 
 The compute runs in ``libfast_infer_b200.so`` (C ABI: include/fast_infer_b200.h).

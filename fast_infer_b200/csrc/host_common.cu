@@ -79,16 +79,19 @@ bool pdl_enabled() {
 }
 
 int sm_count() {
-  static int counts[64] = {0};
+  static std::atomic<int> counts[kMaxCachedDevices];  // zero-initialised (static storage)
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (counts[dev] == 0) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
-      n = 148;
-    counts[dev] = n;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  const bool cached = dev >= 0 && dev < kMaxCachedDevices;
+  if (cached) {
+    const int c = counts[dev].load(std::memory_order_relaxed);
+    if (c > 0) return c;
   }
-  return counts[dev];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    n = 148;
+  if (cached) counts[dev].store(n, std::memory_order_relaxed);  // every writer stores the same n
+  return n;
 }
 
 }  // namespace fi

@@ -6,6 +6,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+
 #include "fast_infer_b200.h"
 
 namespace fi {
@@ -23,8 +26,37 @@ int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, con
                  const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                  CUtensorMapSwizzle swizzle, const char* what);
 
-// Multiprocessor count of the current device (cached per device).
+// Multiprocessor count of the current device (cached per device, thread-safe).
 int sm_count();
+
+// Devices whose per-device set-up results are cached; set-up on a device with a
+// higher index runs on every call instead.
+constexpr int kMaxCachedDevices = 64;
+
+// One-time set-up per device (e.g. cudaFuncSetAttribute, which applies to the
+// current device only). run(fn) calls fn once for the current device and returns
+// its status; concurrent first calls on one device wait for the one that runs it,
+// and a set-up that failed runs again on the next call.
+class DeviceOnce {
+ public:
+  template <typename F>
+  cudaError_t run(F&& fn) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxCachedDevices) return fn();
+    if (done_[dev].load(std::memory_order_acquire)) return cudaSuccess;
+    std::lock_guard<std::mutex> lock(mu_);
+    if (done_[dev].load(std::memory_order_relaxed)) return cudaSuccess;
+    e = fn();
+    if (e == cudaSuccess) done_[dev].store(true, std::memory_order_release);
+    return e;
+  }
+
+ private:
+  std::mutex mu_;
+  std::atomic<bool> done_[kMaxCachedDevices] = {};
+};
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

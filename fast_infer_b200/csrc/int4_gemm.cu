@@ -440,16 +440,14 @@ constexpr size_t i4_smem_x_max() {
 template <int NT, bool kSmemX, int G>
 static int launch_int4_gemm(cudaStream_t st, const CUtensorMap& tm, const CUtensorMap& tms,
                             const I4Args& a) {
-  static bool attr_done[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
-  if (!attr_done[dev]) {
-    const int max_smem = (int)(i4_smem_base<NT, G>() + (kSmemX ? i4_smem_x_max<NT, G>() : 0));
-    cudaError_t e = cudaFuncSetAttribute(int4_gemm_kernel<NT, kSmemX, G>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  static DeviceOnce attr_once;
+  {
+    const cudaError_t e = attr_once.run([] {
+      const int max_smem = (int)(i4_smem_base<NT, G>() + (kSmemX ? i4_smem_x_max<NT, G>() : 0));
+      return cudaFuncSetAttribute(int4_gemm_kernel<NT, kSmemX, G>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+    });
     if (e != cudaSuccess) return cuda_fail(e, "fi_int4_gemm: cudaFuncSetAttribute");
-    attr_done[dev] = true;
   }
   const size_t smem =
       i4_smem_base<NT, G>() + (kSmemX ? (size_t)a.M * (size_t)a.xstride * 2 : 0);

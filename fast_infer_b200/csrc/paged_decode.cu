@@ -529,17 +529,17 @@ extern "C" int fi_paged_decode(const void* q, const void* k_cache, const void* v
   p.scale_log2 = (float)((double)sm_scale * 1.4426950408889634);
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  static bool attr_done[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(
-        paged_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, dec_smem_bytes(1));
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(paged_decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               dec_smem_bytes(2));
+  static DeviceOnce attr_once;
+  {
+    const cudaError_t e = attr_once.run([] {
+      cudaError_t r = cudaFuncSetAttribute(
+          paged_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, dec_smem_bytes(1));
+      if (r == cudaSuccess)
+        r = cudaFuncSetAttribute(paged_decode_kernel<2>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, dec_smem_bytes(2));
+      return r;
+    });
     if (e != cudaSuccess) return cuda_fail(e, "fi_paged_decode: cudaFuncSetAttribute");
-    attr_done[dev] = true;
   }
   dim3 grid((unsigned)max_splits, (unsigned)num_kv_heads, (unsigned)batch);
   // At most one CTA per SM: two page groups per CTA (see paged_decode_kernel).

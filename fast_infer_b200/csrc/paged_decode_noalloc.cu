@@ -20,7 +20,10 @@
 //   workspaces.
 // * The first call on each device resolves the array's device address with
 //   cudaGetSymbolAddress (that device current); make that first call before any
-//   stream capture.
+//   stream capture. The address is kept per device together with the unique ID of
+//   the CUDA context it was resolved in: a call from another context on that device
+//   (after cudaDeviceReset, or a caller's own non-primary context) resolves it again
+//   in that context, which is then a first call too.
 #include <mutex>
 
 #include "common.cuh"
@@ -32,11 +35,43 @@ constexpr int kNoAllocMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_decode_scratch[FI_NOALLOC_SCRATCH_BYTES];
 
-static std::mutex g_scratch_mu;
-static void* g_scratch_ptr[kNoAllocMaxDevices] = {nullptr};
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
 
-// Device address of g_decode_scratch on the current device (resolved once per
-// device). In host code the symbol name is only a host-side stand-in.
+// Unique ID of the calling thread's current CUDA context (cuCtxGetId: never reused
+// within a process, unlike the context handle). False if there is none or the
+// driver lacks the call.
+static bool current_context_id(unsigned long long* id) {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  if (!get_current || !get_id) return false;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return false;
+  return get_id(ctx, id) == CUDA_SUCCESS;
+}
+
+struct ScratchAddress {
+  unsigned long long ctx_id;  // context the address was resolved in
+  void* ptr;                  // nullptr: not resolved yet
+};
+static std::mutex g_scratch_mu;
+static ScratchAddress g_scratch[kNoAllocMaxDevices] = {};
+
+// Device address of g_decode_scratch in the current device's current context
+// (resolved once per device and context). In host code the symbol name is only a
+// host-side stand-in, never a device address.
 static int scratch_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -44,13 +79,20 @@ static int scratch_address(void** out) {
   if (dev < 0 || dev >= kNoAllocMaxDevices)
     return fail(FI_ERR_UNSUPPORTED, "fi_paged_decode_noalloc: device index %d out of range", dev);
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_ptr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_decode_scratch);
-    if (e != cudaSuccess) return cuda_fail(e, "fi_paged_decode_noalloc: cudaGetSymbolAddress");
-    g_scratch_ptr[dev] = p;
+  unsigned long long id = 0;
+  bool have_id = current_context_id(&id);
+  ScratchAddress& c = g_scratch[dev];
+  if (have_id && c.ptr != nullptr && c.ctx_id == id) {
+    *out = c.ptr;
+    return FI_OK;
   }
-  *out = g_scratch_ptr[dev];
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_decode_scratch);
+  if (e != cudaSuccess) return cuda_fail(e, "fi_paged_decode_noalloc: cudaGetSymbolAddress");
+  if (!have_id) have_id = current_context_id(&id);  // the lookup may have made the context
+  // without a context ID nothing is cached: the next call looks the address up again
+  c = have_id ? ScratchAddress{id, p} : ScratchAddress{0, nullptr};
+  *out = p;
   return FI_OK;
 }
 

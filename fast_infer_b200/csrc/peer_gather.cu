@@ -170,6 +170,12 @@ extern "C" int fi_peer_gather(const void* src, int64_t rows, int64_t row_bytes,
                 (long long)rank);
   if (rows < 0 || rows > max_rows || row_bytes <= 0 || nbuf <= 0 || buffer < 0 || buffer >= nbuf)
     return fail(FI_ERR_INVALID_ARG, "fi_peer_gather: bad sizes or buffer index");
+  // A rank that has received every word of call k may start call k+1 while a slower
+  // rank still reads call k's landing area; with one buffer its sends would overwrite
+  // words the slower rank has not read yet.
+  if (world > 1 && nbuf < 2)
+    return fail(FI_ERR_INVALID_ARG, "fi_peer_gather: %lld ranks need at least 2 buffers",
+                (long long)world);
   if (row_bytes % 16 != 0 || src_row_stride_bytes % 16 != 0 || !aligned16(src))
     return fail(FI_ERR_ALIGNMENT,
                 "fi_peer_gather: rows must be 16-byte aligned multiples of 16 bytes");

@@ -547,14 +547,13 @@ static int launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const CU
   if (units > 0x7fffffff) return fail(FI_ERR_UNSUPPORTED, "fi_prefill_fwd: too many work units");
   p.units = (int)units;
   const int grid = (int)(units < sm_count() ? units : sm_count());
-  static bool attr_done[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(prefill_fwd_kernel<kPacked>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmemBytes);
+  static DeviceOnce attr_once;
+  {
+    const cudaError_t e = attr_once.run([] {
+      return cudaFuncSetAttribute(prefill_fwd_kernel<kPacked>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmemBytes);
+    });
     if (e != cudaSuccess) return cuda_fail(e, "fi_prefill_fwd: cudaFuncSetAttribute");
-    attr_done[dev] = true;
   }
   prefill_fwd_kernel<kPacked><<<(unsigned)grid, kPfThreads, kPfSmemBytes,
                                 static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);

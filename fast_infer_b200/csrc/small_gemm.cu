@@ -263,15 +263,13 @@ __global__ void __launch_bounds__(kSgThreads, 1)
 template <int NT>
 static int launch_small_gemm(cudaStream_t st, const CUtensorMap& tm, const SgArgs& a,
                              size_t smem) {
-  static bool attr_done[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
-  if (!attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(small_gemm_kernel<NT>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+  static DeviceOnce attr_once;
+  {
+    const cudaError_t e = attr_once.run([] {
+      return cudaFuncSetAttribute(small_gemm_kernel<NT>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+    });
     if (e != cudaSuccess) return cuda_fail(e, "fi_small_gemm: cudaFuncSetAttribute");
-    attr_done[dev] = true;
   }
   const int items = (a.N + kSgRows - 1) / kSgRows;
   int grid = sm_count();
@@ -548,16 +546,14 @@ __global__ void __launch_bounds__(kSgThreads, kSsStages == 2 ? 3 : 2)
 template <int NT, bool kFold, bool kRope, int kS>
 static int launch_small_gemm_stream_s(cudaStream_t st, const CUtensorMap& tw,
                                       const CUtensorMap& tx, const SsArgs& a) {
-  static bool attr_done[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
   constexpr size_t smem = ss_smem_bytes<NT, kS>();
-  if (!attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(small_gemm_stream_kernel<NT, kFold, kRope, kS>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  static DeviceOnce attr_once;
+  {
+    const cudaError_t e = attr_once.run([] {
+      return cudaFuncSetAttribute(small_gemm_stream_kernel<NT, kFold, kRope, kS>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    });
     if (e != cudaSuccess) return cuda_fail(e, "fi_small_gemm: cudaFuncSetAttribute");
-    attr_done[dev] = true;
   }
   int nb = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, small_gemm_stream_kernel<NT, kFold, kRope, kS>,

@@ -110,7 +110,8 @@ class PeerGather:
     region and waits until every rank has delivered the same call; it returns this
     rank's buffer as [rows, world * row_elems], heads in their original order. Every
     rank must make the same sequence of calls, and two uses of one buffer need another
-    gather between them (the stack uses one buffer per layer). Construct it on every
+    gather between them, so more than one rank needs ``nbuf >= 2`` (the stack uses one
+    buffer per layer and at least two layers). Construct it on every
     rank at the same point (it runs collectives); call ``close`` before the process
     group goes away.
     """
@@ -124,6 +125,9 @@ class PeerGather:
         self.rank = dist.get_rank(group)
         if self.world > 8:
             raise ValueError("PeerGather supports up to 8 ranks")
+        if self.world > 1 and nbuf < 2:
+            # a rank one call ahead would overwrite words a slower rank has not read
+            raise ValueError(f"PeerGather over {self.world} ranks needs nbuf >= 2, got {nbuf}")
         self.device = torch.device(device or "cuda")
         self.max_rows, self.row_elems, self.nbuf = max_rows, row_elems, nbuf
         self._lib = lib = _lib.load()

@@ -126,7 +126,7 @@ class AttentionStack:
         if self.world == 1:
             return o
         if layer is not None and self._peer is not None:
-            return self._peer.gather(o, layer)  # one buffer per layer
+            return self._peer.gather(o, layer % self._peer.nbuf)  # one buffer per layer
         return self.gather(o)
 
     @staticmethod
@@ -178,7 +178,7 @@ class AttentionStack:
             self._h_in = torch.zeros(B, 1, self.hidden, dtype=torch.float16, device=self.device)
             self._graph = None
             if self._peer_wanted and self._peer is None:
-                self._peer = PeerGather(B, self.shard.num_q_heads * self.D, self.L,
+                self._peer = PeerGather(B, self.shard.num_q_heads * self.D, max(self.L, 2),
                                         device=self.device)
 
     def _decode_body(self):

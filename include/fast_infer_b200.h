@@ -150,7 +150,10 @@ int fi_paged_decode(const void* q, const void* k_cache, const void* v_cache, voi
  * Every GPU that loads the library holds the array until exit; all calls on a
  * device share it, so calls that overlap on the GPU race (order them on one
  * stream). The first call on a device looks up the array's device address
- * (cudaGetSymbolAddress); make it before any stream capture.
+ * (cudaGetSymbolAddress); make it before any stream capture. The address is kept
+ * per device and CUDA context: the first call from another context on that device
+ * (after cudaDeviceReset, or a non-primary context of the caller's) looks it up
+ * again, so it too belongs before any capture.
  */
 #define FI_NOALLOC_SCRATCH_BYTES (16 * 1024 * 1024)
 int fi_paged_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, void* o,
@@ -364,7 +367,8 @@ int fi_qkv_rope_kv_write(const void* x, const void* w_rope, float eps, int64_t b
  * On return of the kernel this rank's buffer holds [rows, world * row_bytes] with rank
  * p's block at p. Calls are counted on the device, so a CUDA graph replays correctly;
  * every rank must make the same sequence of calls, and two uses of one buffer need
- * another gather between them. world <= 8. A call whose error_flag already holds
+ * another gather between them, so world > 1 needs nbuf >= 2 (FI_ERR_INVALID_ARG
+ * otherwise). world <= 8. A call whose error_flag already holds
  * FI_DEVERR_TIMEOUT does not wait (pass one persistent word to every call so a broken
  * rendezvous costs one time-out).
  */

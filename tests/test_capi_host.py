@@ -257,6 +257,8 @@ def test_peer_gather_host_checks():
     assert gather(world=0) == bad and gather(world=9) == bad
     assert gather(rank=2) == bad and gather(rank=-1) == bad
     assert gather(rows=17) == bad and gather(buffer=2) == bad and gather(nbuf=0) == bad
+    # two or more ranks need two buffers: a rank one call ahead writes the other one
+    assert gather(nbuf=1) == bad and "at least 2 buffers" in lib.fi_last_error().decode()
     assert gather(row_bytes=24) == _lib.FI_ERR_ALIGNMENT
     assert gather(stride=264) == _lib.FI_ERR_ALIGNMENT
     assert gather() == bad                      # null source rows

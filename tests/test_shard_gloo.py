@@ -81,3 +81,38 @@ def test_kv_head_partition_allgather_matches_unsharded():
     from oracle.attention_oracle import attention_fp32
     ref = attention_fp32(q, k, v).transpose(0, 2, 1, 3).reshape(B, S, Hq * D)
     assert np.array_equal(full, ref)
+
+
+def _peer_nbuf_worker(rank, world, port, result_q):
+    import torch.distributed as dist
+    from fast_infer_b200.shard import PeerGather
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        try:
+            PeerGather(16, 768, nbuf=1, device="cpu")
+            result_q.put((rank, "accepted"))
+        except ValueError as e:
+            result_q.put((rank, str(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_gather_rejects_one_buffer_over_two_ranks():
+    """Two ranks with one gather buffer: the constructor refuses before it allocates
+    or maps anything (a rank one call ahead would overwrite the words a slower rank
+    is still reading)."""
+    ctx = mp.get_context("spawn")
+    result_q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_nbuf_worker, args=(r, 2, port, result_q))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(result_q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r in range(2):
+        assert "nbuf >= 2" in got[r], got[r]
