@@ -265,7 +265,11 @@ def run_ours(args):
     with ClockSampler(local) as clk:
         ms = timed(torch, step, args.steps, args.warmup, dist)
     ms_step = ms / args.steps
-    total_bytes = wl.bytes * world
+    total_bytes = wl.bytes
+    if dist is not None:  # every rank draws its own lengths: sum the job's bytes
+        t = torch.tensor([wl.bytes], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        total_bytes = float(t.item())
     value = total_bytes / (ms_step * 1e-3) / 1e9
 
     # dominant op alone (paged decode + combine), for the roofline
@@ -344,6 +348,7 @@ def run_ours(args):
                "frac_per_gpu": round(gbs5 / world / hbm_peak, 4),
                "tokens_per_s": round(DECODE_SEQS / (ms5 * 1e-3), 1)}
         del wl5
+        kvh["vs_unsharded"] = kvh_vs_unsharded(torch, dev, rank, world, dist)
 
     stack = run_stack(torch, dev, rank, world, dist) if not args.no_stack else None
     int4 = run_int4(torch, dev, max(args.steps // 8, 20), args.warmup, hbm_peak,
@@ -409,13 +414,67 @@ def run_ours(args):
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline_decode(wl.lens, threads=1)
+        result["cpu_baseline"] = cpu_baseline_decode()
+        result["cpu_baselines"] = [result["cpu_baseline"], cpu_baseline_decode_sdpa()] + (
+            reference_interpret_records(["config5_decode", "config3_decode",
+                                         "config1_decode"]) or [])
         result["prefill"]["cpu_baseline"] = cpu_baseline_prefill()
+        result["prefill"]["cpu_baselines"] = [result["prefill"]["cpu_baseline"]] + (
+            reference_interpret_records(["config2_prefill", "config1_prefill"]) or [])
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(result))
+
+
+# north_star tolerances (max-abs, relative L2) for the floating-point outputs
+TOL_MAX_ABS, TOL_REL_L2 = 2e-3, 1e-3
+
+
+def _err(torch, out, ref):
+    """(max-abs, relative-L2) of out against ref, in float64."""
+    o, r = out.double(), ref.double()
+    den = r.norm().item()
+    return (o - r).abs().max().item(), ((o - r).norm().item() / den if den > 0 else 0.0)
+
+
+def _reduce(torch, dev, dist, vals, op):
+    if dist is None:
+        return vals
+    t = torch.tensor(vals, dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=op)
+    return t.tolist()
+
+
+def kvh_vs_unsharded(torch, dev, rank, world, dist):
+    """Correctness of the KV-head partition on the config-5 shape: every rank runs the
+    unsharded decode (8 KV heads, 24 query heads) of one layer of identical data and
+    its own shard (KV heads [r*8/N, (r+1)*8/N) of the same pages, their query heads)
+    through the same entry point, and compares the shard's heads with the unsharded
+    output's. Outside the timed region; reduced over ranks."""
+    if world == 1:
+        return None
+    from fast_infer_b200.kernels.attention import paged_attention
+    from fast_infer_b200.shard import head_shard
+    wl = DecodeWorkload(torch, dev, DECODE_SEQS, DECODE_LO, DECODE_HI, DECODE_SEED, 1)
+    full = wl.attend(0)
+    sh = head_shard(rank, world, HQ, HKV)
+    nkv = sh.num_kv_heads
+    part = paged_attention(wl.q[:, sh.q_start:sh.q_end], wl.k[0].narrow(2, sh.kv_start, nkv),
+                           wl.v[0].narrow(2, sh.kv_start, nkv), wl.bt, BS, 0,
+                           context_lens=wl.ctx, max_context_len=wl.max_ctx)
+    ref = full[:, sh.q_start:sh.q_end]
+    torch.cuda.synchronize()
+    same = 1.0 if torch.equal(part, ref) else 0.0
+    max_abs, rel = _err(torch, part, ref)
+    del wl
+    max_abs, rel = _reduce(torch, dev, dist, [max_abs, rel], dist.ReduceOp.MAX)
+    (same,) = _reduce(torch, dev, dist, [same], dist.ReduceOp.MIN)
+    return {"bitexact": same == 1.0, "max_abs": max_abs, "rel_l2": rel,
+            "ok": max_abs <= TOL_MAX_ABS and rel <= TOL_REL_L2,
+            "what": "each rank's KV-head shard of one config-5 layer vs the unsharded decode "
+                    "of the same data on that rank (worst rank)"}
 
 
 def prefill_inputs(torch, dev, nsets):
@@ -479,10 +538,10 @@ def run_only(args):
         c3 = args.only == "decode_c3"
         wl = DecodeWorkload(torch, dev, C3_SEQS if c3 else DECODE_SEQS, C3_LO if c3 else DECODE_LO,
                             C3_HI if c3 else DECODE_HI, C3_SEED if c3 else DECODE_SEED,
-                            args.layers)
+                            args.layers, hkv=args.hkv)
         ms = timed(torch, lambda i: wl.attend(i % args.layers), args.steps, args.warmup) / args.steps
         gbs = wl.bytes / (ms * 1e-3) / 1e9
-        out.update(ms=round(ms, 4), gbs=round(gbs, 1), bytes=wl.bytes,
+        out.update(ms=round(ms, 4), gbs=round(gbs, 1), bytes=wl.bytes, kv_heads=args.hkv,
                    frac=round(gbs / float(peaks["hbm_gbs"]), 4))
     print(json.dumps(out))
 
@@ -547,8 +606,7 @@ def run_stack(torch, dev, rank, world, dist, warmup=1):
     dec_ms = max_ms(e[0].elapsed_time(e[1]))
     finite = bool(torch.isfinite(h).all().item())
     peer_errors = st._peer.errors() if st._peer is not None else 0
-    st.close()
-    sync_all()
+    checks = stack_checks(torch, dev, rank, world, dist, st, prompt, use_graph, sync_all)
     return {
         "workload": "config 4: 28-layer attention stack (Llama-3.2-3B attention shapes, random "
                     "weights), B16, prefill 1024 then 256 decode steps, KV heads sharded over "
@@ -563,7 +621,69 @@ def run_stack(torch, dev, rank, world, dist, warmup=1):
         "cuda_graph": use_graph,
         "finite": finite,
         "peer_gather_errors": peer_errors,
+        **checks,
     }
+
+
+STACK_CHECK_PROMPT, STACK_CHECK_STEPS = 256, 8
+
+
+def stack_checks(torch, dev, rank, world, dist, st, prompt, use_graph, sync_all):
+    """Correctness of the sharded stack, outside the timed region (closes ``st``).
+
+    * gather_bitexact: after a CUDA-graph decode, every rank's peer-memory gather
+      buffer of every layer equals the NCCL all-gather of each rank's own block
+      (order of the head blocks, and no word of an older call).
+    * ranks_identical: every rank holds the same hidden state.
+    * stack_vs_n1: rank 0 runs the same prompt and decode steps through an unsharded
+      stack (one GPU, same seed) and compares the decode outputs. Tolerance: relative
+      L2 <= 1e-3 and max-abs <= 2e-3 x max|output| (the max-abs
+      scaled to the hidden state's magnitude, which grows over 28 residual layers).
+    At N = 1 only the stack itself ran; the three entries are null."""
+    from fast_infer_b200.shard import gather_heads
+    from fast_infer_b200.stack import AttentionStack
+    if world == 1:
+        st.close()
+        sync_all()
+        return {"gather_bitexact": None, "ranks_identical": None, "stack_vs_n1": None}
+    out_n = st.generate(prompt[:, :STACK_CHECK_PROMPT], STACK_CHECK_STEPS, use_graph=use_graph)
+    same = 1.0
+    if st._peer is not None:
+        w = st._peer.row_elems
+        for li in range(st._peer.nbuf):
+            buf = st._peer.result(li, st.batch)
+            ref = gather_heads(buf[:, rank * w:(rank + 1) * w].contiguous())
+            if not torch.equal(buf, ref):
+                same = 0.0
+    (gather_ok,) = _reduce(torch, dev, dist, [same], dist.ReduceOp.MIN)
+    r0 = out_n.clone()
+    dist.broadcast(r0, 0)
+    (ident,) = _reduce(torch, dev, dist, [1.0 if torch.equal(r0, out_n) else 0.0],
+                       dist.ReduceOp.MIN)
+    had_peer = st._peer is not None
+    st.close()
+    del st
+    torch.cuda.empty_cache()
+    vs = None
+    if rank == 0:
+        one = AttentionStack(num_layers=STACK_LAYERS, batch=STACK_BATCH,
+                             max_seq_len=STACK_PROMPT + STACK_STEPS, rank=0, world=1,
+                             device=dev, seed=4)
+        out_1 = one.generate(prompt[:, :STACK_CHECK_PROMPT], STACK_CHECK_STEPS,
+                             use_graph=use_graph)
+        max_abs, rel = _err(torch, out_n, out_1)
+        scale = out_1.abs().max().item()
+        vs = {"max_abs": max_abs, "rel_l2": rel, "max_abs_ref": scale,
+              "ok": rel <= TOL_REL_L2 and max_abs <= TOL_MAX_ABS * max(1.0, scale),
+              "what": f"decode outputs of {STACK_CHECK_STEPS} steps after a "
+                      f"{STACK_CHECK_PROMPT}-token prompt (B{STACK_BATCH}, 28 layers), "
+                      f"{world}-GPU sharded stack vs the unsharded stack on one GPU"}
+        one.close()
+        del one
+        torch.cuda.empty_cache()
+    sync_all()
+    return {"gather_bitexact": (gather_ok == 1.0) if had_peer else None,
+            "ranks_identical": ident == 1.0, "stack_vs_n1": vs}
 
 
 def int4_weight_bytes(n, k):
@@ -642,51 +762,170 @@ def _needs_combine(wl):
 
 
 # --------------------------------------------------------- CPU baselines
-def _cpu_decode_chunk(args):
-    seed, idx, lens = args
+# The decode CPU baselines (the oracle port in both arms, PyTorch SDPA) run on one fixed,
+# stated sample of the config-5-shaped workload: every CPU_SAMPLE_STEP-th sequence of the
+# 256 (seed-3 lengths), i.e. 64 sequences whose pages and query come from per-sequence
+# seeds. The port runs one worker process per host core (at most one per sequence).
+CPU_SAMPLE_STEP = 4
+
+
+def cpu_sample():
+    """(indices, lengths) of the decode CPU sample."""
+    lens = ragged_lens(DECODE_SEQS, DECODE_LO, DECODE_HI, DECODE_SEED)
+    idx = np.arange(0, DECODE_SEQS, CPU_SAMPLE_STEP)
+    return idx, lens[idx]
+
+
+def _ref_inputs(idx):
+    """Sequence ``idx`` of the decode workload for the CPU baselines: pages and query
+    from a per-sequence seed (the length is the workload's)."""
+    n = int(ragged_lens(DECODE_SEQS, DECODE_LO, DECODE_HI, DECODE_SEED)[idx])
+    rng = np.random.default_rng(10_000 + idx)
+    pages = (n + BS - 1) // BS
+    kc = rng.standard_normal((pages, BS, HKV, D), dtype=np.float32).astype(np.float16)
+    vc = rng.standard_normal((pages, BS, HKV, D), dtype=np.float32).astype(np.float16)
+    q = rng.standard_normal((1, HQ, D), dtype=np.float32).astype(np.float16)
+    bt = rng.permutation(pages).astype(np.int32)[None]
+    return q, kc, vc, bt, np.array([n], np.int32)
+
+
+def _ref_worker(conn, seqs):
+    """One host core: owns the sample sequences ``seqs``; runs their paged decode with
+    the CPU oracle (the reference's per-page online-softmax algorithm restated in
+    numpy) once per step message and replies with their algorithmic bytes."""
     from oracle.attention_oracle import paged_attention_vectorized
-    rng = np.random.default_rng(seed)
-    sub = np.asarray(lens)[idx]
-    bt, total = make_tables(sub, rng)
-    kc = rng.standard_normal((total, BS, HKV, D), dtype=np.float32).astype(np.float16)
-    vc = rng.standard_normal((total, BS, HKV, D), dtype=np.float32).astype(np.float16)
-    q = rng.standard_normal((len(sub), HQ, D), dtype=np.float32).astype(np.float16)
-    t0 = time.perf_counter()
-    paged_attention_vectorized(q, kc, vc, bt, BS, sub)
-    return time.perf_counter() - t0, decode_bytes(sub)
+    inputs = [_ref_inputs(int(i)) for i in seqs]
+    nbytes = sum(decode_bytes(x[4]) for x in inputs)
+    conn.send("ready")
+    while True:
+        msg = conn.recv()
+        if msg is None:
+            break
+        for q, kc, vc, bt, lens in inputs:
+            paged_attention_vectorized(q, kc, vc, bt, BS, lens)
+        conn.send(nbytes)
 
 
-def cpu_baseline_decode(lens, threads=1, budget_s=12.0):
-    """Time the CPU oracle (per-block online-softmax decode in numpy) on a bounded
-    sample of the workload's sequences; returns GB/s of algorithmic bytes."""
-    lens = np.asarray(lens)
-    n = len(lens)
-    # grow the sample until it costs ~budget_s of CPU time (cap: whole batch)
-    sample = 8
-    done_s, done_b, used = 0.0, 0.0, 0
-    if threads <= 1:
-        while used < n and done_s < budget_s:
-            idx = np.arange(used, min(n, used + sample))
-            s, b = _cpu_decode_chunk((used, idx, lens))
-            done_s += s
-            done_b += b
-            used += len(idx)
-            sample *= 2
-        secs = done_s
-    else:
-        import multiprocessing as mp
-        ctx = mp.get_context("spawn")
-        chunks = [(i, np.arange(i, min(n, i + 4)), lens) for i in range(0, n, 4)]
+def cpu_decode_port(steps, warmup):
+    """The oracle port on the CPU sample, one worker process per host core; returns
+    (GB/s, seconds per step, workers). Workers are spawned (the caller may already
+    have initialised CUDA)."""
+    import multiprocessing as mp
+    idx, _ = cpu_sample()
+    workers = max(1, min(os.cpu_count() or 1, len(idx)))
+    saved = {v: os.environ.get(v) for v in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS",
+                                            "MKL_NUM_THREADS")}
+    for var in saved:
+        os.environ[var] = "1"  # the parallelism is one process per core
+    ctx = mp.get_context("spawn")
+    pipes, procs = [], []
+    try:
+        for w in range(workers):
+            a, b = ctx.Pipe()
+            pr = ctx.Process(target=_ref_worker, args=(b, idx[w::workers].tolist()), daemon=True)
+            pr.start()
+            pipes.append(a)
+            procs.append(pr)
+    finally:
+        for var, val in saved.items():
+            if val is None:
+                os.environ.pop(var, None)
+            else:
+                os.environ[var] = val
+    try:
+        for c in pipes:
+            c.recv()
+
+        def step():
+            for c in pipes:
+                c.send(1)
+            return sum(c.recv() for c in pipes)
+
+        for _ in range(warmup):
+            step()
         t0 = time.perf_counter()
-        with ctx.Pool(threads) as pool:
-            res = pool.map(_cpu_decode_chunk, chunks)
+        total = 0.0
+        for _ in range(steps):
+            total += step()
         secs = time.perf_counter() - t0
-        done_b = sum(r[1] for r in res)
-        used = n
-    return {"value": round(done_b / secs / 1e9, 4), "unit": "GB/s", "cores": threads,
+    finally:
+        for c in pipes:
+            c.send(None)
+        for pr in procs:
+            pr.join(timeout=30)
+    return total / secs / 1e9, secs / max(1, steps), workers
+
+
+def _sample_desc():
+    idx, sub = cpu_sample()
+    lens = ragged_lens(DECODE_SEQS, DECODE_LO, DECODE_HI, DECODE_SEED)
+    return (f"every {CPU_SAMPLE_STEP}th sequence of the config-5-shaped decode batch "
+            f"({len(idx)} of {DECODE_SEQS}, mean context {sub.mean():.0f} vs {lens.mean():.0f} "
+            f"for the batch), one layer")
+
+
+def cpu_baseline_decode(steps=3, warmup=1):
+    """The oracle port (numpy, the reference's decode algorithm) on the CPU sample with
+    every host core, the same sample and cores as the reference arm."""
+    gbs, step_s, workers = cpu_decode_port(steps, warmup)
+    return {"value": round(gbs, 4), "unit": "GB/s", "cores": workers, "kind": "port",
+            "sample": f"{_sample_desc()}; numpy oracle paged_attention_vectorized, one worker "
+                      f"process per core; {step_s:.3f} s per pass"}
+
+
+def cpu_baseline_decode_sdpa(reps=2):
+    """The PyTorch SDPA CPU equivalent of the decode on the CPU sample: per sequence,
+    fp32 ``scaled_dot_product_attention(enable_gqa=True)`` of its query over its
+    gathered pages (all host threads); best of ``reps`` passes."""
+    import torch
+    ncores = os.cpu_count() or 1
+    torch.set_num_threads(ncores)
+    idx, _ = cpu_sample()
+    data, nbytes = [], 0.0
+    for i in idx:
+        q, kc, vc, bt, lens = _ref_inputs(int(i))
+        n = int(lens[0])
+        order = torch.from_numpy(bt[0].astype(np.int64))
+        k = torch.from_numpy(kc).float()[order].reshape(-1, HKV, D)[:n].transpose(0, 1)[None]
+        v = torch.from_numpy(vc).float()[order].reshape(-1, HKV, D)[:n].transpose(0, 1)[None]
+        data.append((torch.from_numpy(q).float()[:, :, None], k.contiguous(), v.contiguous()))
+        nbytes += decode_bytes(lens)
+    best = float("inf")
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        for q, k, v in data:
+            torch.nn.functional.scaled_dot_product_attention(q, k, v, enable_gqa=True)
+        best = min(best, time.perf_counter() - t0)
+    return {"value": round(nbytes / best / 1e9, 4), "unit": "GB/s", "cores": ncores,
             "kind": "port",
-            "sample": f"{used} of {n} sequences of the decode workload (one layer), numpy "
-                      f"oracle paged_attention_vectorized, {secs:.1f} s"}
+            "sample": f"{_sample_desc()}; fp32 PyTorch scaled_dot_product_attention("
+                      f"enable_gqa) per sequence over its gathered pages, best of {reps}: "
+                      f"{best:.3f} s"}
+
+
+def reference_interpret_records(which):
+    """The reference's own Triton kernels timed under TRITON_INTERPRET=1, as recorded by
+    oracle/time_reference_interpret.py where the reference checkout is (it does not
+    travel to the GPU box): the host, core count and sample it states."""
+    path = os.path.join(ROOT, "oracle", "reference_interpret_timing.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        rec = json.load(f)
+    out = []
+    for name in which:
+        e = rec["entries"].get(name)
+        if e is None:
+            continue
+        unit = "TFLOP/s" if "tflops" in e else "GB/s"
+        out.append({"value": round(e["tflops"] if "tflops" in e else e["gbs"], 6), "unit": unit,
+                    "cores": rec["cores"], "kind": "reference-triton-interpret",
+                    "workload": name, "extrapolated": e["extrapolated"],
+                    "sample": e["sample"],
+                    "measured_on": f"{rec['host_cpu']} ({rec['cores']} cores; recorded "
+                                   f"{rec['when']}, not this box: the reference checkout "
+                                   f"stays where it was timed)"})
+    return out
 
 
 def cpu_baseline_prefill(reps=2):
@@ -714,95 +953,32 @@ def cpu_baseline_prefill(reps=2):
                       f"best of {reps}: {best:.2f} s"}
 
 
-def _ref_inputs(idx):
-    """Sequence ``idx`` of the decode workload for the CPU reference arm: pages and
-    query from a per-sequence seed (the lengths are the workload's)."""
-    n = int(ragged_lens(DECODE_SEQS, DECODE_LO, DECODE_HI, DECODE_SEED)[idx])
-    rng = np.random.default_rng(10_000 + idx)
-    pages = (n + BS - 1) // BS
-    kc = rng.standard_normal((pages, BS, HKV, D), dtype=np.float32).astype(np.float16)
-    vc = rng.standard_normal((pages, BS, HKV, D), dtype=np.float32).astype(np.float16)
-    q = rng.standard_normal((1, HQ, D), dtype=np.float32).astype(np.float16)
-    bt = rng.permutation(pages).astype(np.int32)[None]
-    return q, kc, vc, bt, np.array([n], np.int32)
-
-
-def _ref_worker(conn, idx):
-    """One host core of the reference arm: owns sequence ``idx``; runs its paged
-    decode with the CPU oracle once per step message, replies with the bytes."""
-    from oracle.attention_oracle import paged_attention_vectorized
-    q, kc, vc, bt, lens = _ref_inputs(idx)
-    nbytes = decode_bytes(lens)
-    conn.send("ready")
-    while True:
-        msg = conn.recv()
-        if msg is None:
-            break
-        paged_attention_vectorized(q, kc, vc, bt, BS, lens)
-        conn.send(nbytes)
-
-
 def run_reference(args):
     """Reference arm: the reference's decode algorithm on the host cores. The
     reference implements it only as a Triton kernel (its CPU form is the Triton
-    interpreter, which needs the reference checkout); the oracle's restatement of
-    that algorithm stands in. One worker process per host core owns one sequence of
-    the decode workload; every step runs all of them in parallel (a bounded sample of
-    the workload: as many sequences as cores). Value = algorithmic bytes / wall time
-    over the timed steps."""
+    interpreter, which needs the reference checkout that does not travel to this box);
+    the oracle's restatement of that algorithm stands in. Each step runs the fixed CPU
+    sample of the decode workload (``cpu_sample``) with one worker process per host
+    core. Value = algorithmic bytes / wall time over the timed steps."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import multiprocessing as mp
-    ncores = os.cpu_count() or 1
-    for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
-        os.environ[var] = "1"  # the parallelism is one process per core
-    ctx = mp.get_context("spawn")
-    pipes, procs = [], []
-    for i in range(ncores):
-        a, b = ctx.Pipe()
-        pr = ctx.Process(target=_ref_worker, args=(b, i % DECODE_SEQS), daemon=True)
-        pr.start()
-        pipes.append(a)
-        procs.append(pr)
-    try:
-        for c in pipes:
-            c.recv()
-
-        def step():
-            for c in pipes:
-                c.send(1)
-            return sum(c.recv() for c in pipes)
-
-        for _ in range(args.warmup):
-            step()
-        t0 = time.perf_counter()
-        total = 0.0
-        for _ in range(args.steps):
-            total += step()
-        secs = time.perf_counter() - t0
-    finally:
-        for c in pipes:
-            c.send(None)
-        for pr in procs:
-            pr.join(timeout=30)
-    value = total / secs / 1e9
-    ms_step = secs * 1e3 / max(1, args.steps)
-    sample_desc = (f"per step {ncores} sequences of the config-5-shaped decode workload "
-                   f"(one per core, sequences 0..{ncores - 1}), numpy oracle "
-                   f"paged_attention_vectorized; {args.steps} steps in {secs:.1f} s")
+    value, step_s, workers = cpu_decode_port(args.steps, args.warmup)
+    sample_desc = (f"per step {_sample_desc()}; numpy oracle paged_attention_vectorized, "
+                   f"one worker process per core ({workers})")
     result = {
         "metric": "decode-attn HBM GB/s", "value": round(value, 4), "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms_step, 3), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(step_s * 1e3, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32 (numpy)", "data": "synthetic", "impl": "reference",
         "config": {"workload": "config5-shaped ragged paged decode: 256 seqs, ctx U[1024,4096] "
                                "(seed 3), GQA 24/8, D128, block 64"},
-        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": ncores,
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": workers,
                          "kind": "port", "sample": sample_desc},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
+        "reference_triton_interpret": reference_interpret_records(["config5_decode"]),
     }
     print(json.dumps(result))
 
@@ -820,6 +996,9 @@ def main():
                     help="time one kernel family alone (profiling runs); prints one JSON line")
     ap.add_argument("--layers", type=int, default=DECODE_LAYERS,
                     help="resident KV-cache layers of the decode workload")
+    ap.add_argument("--hkv", type=int, default=HKV,
+                    help="KV heads of the --only decode workloads (with 3x as many query heads): "
+                         "8 / N times the per-rank share of an N-GPU KV-head partition")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -22,7 +22,11 @@
 // * Split-KV (flash-decoding): a sequence's pages are cut into splits of
 //   `pages_per_split`; each split writes (max, sum, unnormalised acc) to the
 //   workspace and a small combine kernel produces the output. With one split the
-//   main kernel writes the output directly.
+//   main kernel writes the output directly. The hardware block scheduler hands
+//   (sequence, KV head, split) CTAs to SMs as earlier ones finish, which balances
+//   ragged lengths better than a static partition of all pages over one wave of
+//   CTAs (measured: that partition pays a ring drain at every unit boundary inside a
+//   CTA and a per-CTA scan of the lengths, and was slower on every shape).
 #include <math.h>
 
 #include "common.cuh"
@@ -35,17 +39,15 @@ constexpr int kPage = 64;
 constexpr int kDecWarps = 4;  // consumer warps of a page group (16 rows each)
 // Threads of a CTA whose kGrp groups of 4 consumer warps take alternate pages.
 __host__ __device__ constexpr int dec_threads(int kgrp) { return (kDecWarps * kgrp + 1) * 32; }
-#ifndef FI_DEC_STAGES
-#define FI_DEC_STAGES 3
-#endif
-constexpr int kDecStages = FI_DEC_STAGES;
+// Ring slots per page group: 3 (two CTAs per SM), or 2 for grids of two to four CTAs
+// per SM, where a third resident CTA per SM puts the working CTAs into one wave.
+constexpr int kDecStages = 3;
 constexpr int kRegionBytes = kPage * 64 * 2;    // 64 rows x 64 fp16
 constexpr int kStageBytes = 4 * kRegionBytes;   // K lo, K hi, V lo, V hi
 constexpr int kMaxPagesPerSplit = 32;
-// Shared memory of a CTA with kgrp page groups, each with its own kDecStages ring.
-__host__ __device__ constexpr int dec_smem_bytes(int kgrp) {
-  return 1024 + kgrp * kDecStages * kStageBytes + 2 * kgrp * kDecStages * 8 +
-         kMaxPagesPerSplit * 4;
+// Shared memory of a CTA with kgrp page groups, each with its own ring of kst slots.
+__host__ __device__ constexpr int dec_smem_bytes(int kgrp, int kst = kDecStages) {
+  return 1024 + kgrp * kst * kStageBytes + 2 * kgrp * kst * 8 + kMaxPagesPerSplit * 4;
 }
 
 struct DecodeParams {
@@ -82,18 +84,119 @@ __device__ __forceinline__ uint32_t swz(uint32_t region, int row, int chunk) {
   return region + row * 128 + ((chunk ^ (row & 7)) << 4);
 }
 
+// The query of (sequence b, KV head kvh) as m16n8k16 B fragments: head slot
+// g = lane/4 holds query head kvh*G + g (zero for g >= G), dims 2*(lane&3) + {0, 1, 8,
+// 9} of every 16-dim step.
+__device__ __forceinline__ void load_q(const DecodeParams& p, int b, int kvh, int lane,
+                                       uint32_t (&qf)[8][2]) {
+  const int g = lane >> 2, tq = lane & 3;
+  const bool hv = g < p.group;
+  const __half* qrow = p.q + b * p.qs[0] + (int64_t)(kvh * p.group + (hv ? g : 0)) * p.qs[1];
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const int d0 = kk * 16 + 2 * tq;
+    float x0 = 0.f, x1 = 0.f, x8 = 0.f, x9 = 0.f;
+    if (hv) {
+      x0 = __half2float(qrow[d0 * p.qs[2]]);
+      x1 = __half2float(qrow[(d0 + 1) * p.qs[2]]);
+      x8 = __half2float(qrow[(d0 + 8) * p.qs[2]]);
+      x9 = __half2float(qrow[(d0 + 9) * p.qs[2]]);
+    }
+    qf[kk][0] = pack_half2(x0, x1);
+    qf[kk][1] = pack_half2(x8, x9);
+  }
+}
+
+// One page of one (sequence, KV head) for a consumer warp: its 16 rows of the page
+// (row_base..row_base+15, `valid` of them live) against the G <= 8 query heads held
+// as m16n8k16 B fragments in qf, folded into the warp's online-softmax state
+// (m0/m1, l0/l1: head slots 2*(lane&3) and +1; acc: [8 dim tiles][4]).
+__device__ __forceinline__ void decode_page(uint32_t st, int row_base, int lane, int valid,
+                                            const uint32_t (&qf)[8][2], float scale_log2,
+                                            float& m0, float& m1, float& l0, float& l1,
+                                            float (&acc)[8][4]) {
+  const int g = lane >> 2;
+  const uint32_t klo = st, khi = st + kRegionBytes;
+  const uint32_t vlo = st + 2 * kRegionBytes, vhi = st + 3 * kRegionBytes;
+  // S^T tile: 16 tokens x 8 head slots, K from shared memory, q^T in registers.
+  float c[4] = {0.f, 0.f, 0.f, 0.f};
+  {
+    const int r = row_base + (lane & 15);
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4(swz(kk < 4 ? klo : khi, r, (kk & 3) * 2 + (lane >> 4)), a0, a1, a2, a3);
+      mma_16816(c, a0, a1, a2, a3, qf[kk][0], qf[kk][1]);
+    }
+  }
+  float s0 = c[0] * scale_log2, s1 = c[1] * scale_log2;
+  float s2 = c[2] * scale_log2, s3 = c[3] * scale_log2;
+  if (g >= valid) s0 = s1 = -INFINITY;
+  if (g + 8 >= valid) s2 = s3 = -INFINITY;
+  float mx0 = fmaxf(s0, s2), mx1 = fmaxf(s1, s3);
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+  }
+  const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+  const float al0 = fast_exp2(m0 - mn0), al1 = fast_exp2(m1 - mn1);
+  const float p0 = fast_exp2(s0 - mn0), p1 = fast_exp2(s1 - mn1);
+  const float p2 = fast_exp2(s2 - mn0), p3 = fast_exp2(s3 - mn1);
+  l0 = l0 * al0 + p0 + p2;
+  l1 = l1 * al1 + p1 + p3;
+  m0 = mn0;
+  m1 = mn1;
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    acc[mt][0] *= al0;
+    acc[mt][1] *= al1;
+    acc[mt][2] *= al0;
+    acc[mt][3] *= al1;
+  }
+  if (valid < 16) {
+    // Rows past the context may hold anything (stale pages): zero this warp's
+    // dead V rows so 0 * (inf/nan) cannot reach the accumulator.
+    const int dead = 16 - valid;
+    for (int idx = lane; idx < dead * 16; idx += 32) {
+      const int row = row_base + valid + (idx >> 4);
+      const int ch = idx & 15;
+      const uint32_t addr = swz(ch < 8 ? vlo : vhi, row, ch & 7);
+      asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0u) : "memory");
+    }
+    __syncwarp();
+  }
+  const uint32_t pb0 = movmatrix_t(pack_half2(p0, p1));
+  const uint32_t pb1 = movmatrix_t(pack_half2(p2, p3));
+  {
+    const int tok = row_base + ((lane >> 4) << 3) + (lane & 7);
+    const int chb = (lane >> 3) & 1;
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4_t(swz(mt < 4 ? vlo : vhi, tok, (mt & 3) * 2 + chb), a0, a1, a2, a3);
+      mma_16816(acc[mt], a0, a1, a2, a3, pb0, pb1);
+    }
+  }
+  // the zeroed rows were written by the generic proxy; the slot's next TMA write
+  // (async proxy) must come after them
+  if (valid < 16) fence_proxy_async_smem();
+}
+
 // kGrp = 2 (grids of at most one CTA per SM): two groups of four consumer warps take
 // alternate pages of the split, so a CTA has two pages in flight through its
 // per-page dependency chain (QK^T, softmax, PV) where one group would leave the SM
 // waiting; the groups' states merge with the warps' at the end. Each group has its
-// own ring (page i -> group i % kGrp, slot (i / kGrp) % kDecStages of that ring), so
+// own ring (page i -> group i % kGrp, slot (i / kGrp) % kSt of that ring), so
 // every waiter is at most one mbarrier phase ahead: with one shared ring a group
 // could wait on a slot two phases ahead, and the parity test would report the
 // previous phase as the one it wants.
-template <int kGrp>
-__global__ void __launch_bounds__(dec_threads(kGrp), kGrp == 1 ? 2 : 1)
+// kSt = ring slots per group: 3 with two CTAs per SM, 2 with three (kGrp = 1 only).
+template <int kGrp, int kSt>
+__global__ void __launch_bounds__(dec_threads(kGrp), kGrp == 1 ? (kSt == 2 ? 3 : 2) : 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const DecodeParams p) {
+  constexpr int kDecStages = kSt;  // shadows the default for this instance
   constexpr int kCW = kDecWarps * kGrp;  // consumer warps
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_align1024(smem_raw);
@@ -171,23 +274,7 @@ __global__ void __launch_bounds__(dec_threads(kGrp), kGrp == 1 ? 2 : 1)
   // ---------------------------------------------------------------- consumers
   const int g = lane >> 2, tq = lane & 3;
   uint32_t qf[8][2];
-  {
-    const bool hv = g < p.group;
-    const __half* qrow = p.q + b * p.qs[0] + (int64_t)(kvh * p.group + (hv ? g : 0)) * p.qs[1];
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      const int d0 = kk * 16 + 2 * tq;
-      float x0 = 0.f, x1 = 0.f, x8 = 0.f, x9 = 0.f;
-      if (hv) {
-        x0 = __half2float(qrow[d0 * p.qs[2]]);
-        x1 = __half2float(qrow[(d0 + 1) * p.qs[2]]);
-        x8 = __half2float(qrow[(d0 + 8) * p.qs[2]]);
-        x9 = __half2float(qrow[(d0 + 9) * p.qs[2]]);
-      }
-      qf[kk][0] = pack_half2(x0, x1);
-      qf[kk][1] = pack_half2(x8, x9);
-    }
-  }
+  load_q(p, b, kvh, lane, qf);
 
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
   float acc[8][4];
@@ -205,70 +292,8 @@ __global__ void __launch_bounds__(dec_threads(kGrp), kGrp == 1 ? 2 : 1)
     }
     const int valid = ctx - (pg0 + i) * kPage - row_base;  // live rows among this warp's 16
     if (s_phys[i] >= 0 && valid > 0) {
-      const uint32_t st = smem_u32(smem + s * kStageBytes);
-      const uint32_t klo = st, khi = st + kRegionBytes;
-      const uint32_t vlo = st + 2 * kRegionBytes, vhi = st + 3 * kRegionBytes;
-      // S^T tile: 16 tokens x 8 head slots, K from shared memory, q^T in registers.
-      float c[4] = {0.f, 0.f, 0.f, 0.f};
-      {
-        const int r = row_base + (lane & 15);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          uint32_t a0, a1, a2, a3;
-          ldsm_x4(swz(kk < 4 ? klo : khi, r, (kk & 3) * 2 + (lane >> 4)), a0, a1, a2, a3);
-          mma_16816(c, a0, a1, a2, a3, qf[kk][0], qf[kk][1]);
-        }
-      }
-      float s0 = c[0] * p.scale_log2, s1 = c[1] * p.scale_log2;
-      float s2 = c[2] * p.scale_log2, s3 = c[3] * p.scale_log2;
-      if (g >= valid) s0 = s1 = -INFINITY;
-      if (g + 8 >= valid) s2 = s3 = -INFINITY;
-      float mx0 = fmaxf(s0, s2), mx1 = fmaxf(s1, s3);
-#pragma unroll
-      for (int off = 4; off < 32; off <<= 1) {
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-      }
-      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-      const float al0 = fast_exp2(m0 - mn0), al1 = fast_exp2(m1 - mn1);
-      const float p0 = fast_exp2(s0 - mn0), p1 = fast_exp2(s1 - mn1);
-      const float p2 = fast_exp2(s2 - mn0), p3 = fast_exp2(s3 - mn1);
-      l0 = l0 * al0 + p0 + p2;
-      l1 = l1 * al1 + p1 + p3;
-      m0 = mn0;
-      m1 = mn1;
-#pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        acc[mt][0] *= al0;
-        acc[mt][1] *= al1;
-        acc[mt][2] *= al0;
-        acc[mt][3] *= al1;
-      }
-      if (valid < 16) {
-        // Rows past the context may hold anything (stale pages): zero this warp's
-        // dead V rows so 0 * (inf/nan) cannot reach the accumulator.
-        const int dead = 16 - valid;
-        for (int idx = lane; idx < dead * 16; idx += 32) {
-          const int row = row_base + valid + (idx >> 4);
-          const int ch = idx & 15;
-          const uint32_t addr = swz(ch < 8 ? vlo : vhi, row, ch & 7);
-          asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0u) : "memory");
-        }
-        __syncwarp();
-      }
-      const uint32_t pb0 = movmatrix_t(pack_half2(p0, p1));
-      const uint32_t pb1 = movmatrix_t(pack_half2(p2, p3));
-      {
-        const int tok = row_base + ((lane >> 4) << 3) + (lane & 7);
-        const int chb = (lane >> 3) & 1;
-#pragma unroll
-        for (int mt = 0; mt < 8; ++mt) {
-          uint32_t a0, a1, a2, a3;
-          ldsm_x4_t(swz(mt < 4 ? vlo : vhi, tok, (mt & 3) * 2 + chb), a0, a1, a2, a3);
-          mma_16816(acc[mt], a0, a1, a2, a3, pb0, pb1);
-        }
-      }
-      if (valid < 16) fence_proxy_async_smem();
+      decode_page(smem_u32(smem + s * kStageBytes), row_base, lane, valid, qf, p.scale_log2, m0,
+                  m1, l0, l1, acc);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
@@ -532,23 +557,36 @@ extern "C" int fi_paged_decode(const void* q, const void* k_cache, const void* v
   static DeviceOnce attr_once;
   {
     const cudaError_t e = attr_once.run([] {
-      cudaError_t r = cudaFuncSetAttribute(
-          paged_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, dec_smem_bytes(1));
+      cudaError_t r = cudaFuncSetAttribute(paged_decode_kernel<1, 3>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           dec_smem_bytes(1, 3));
       if (r == cudaSuccess)
-        r = cudaFuncSetAttribute(paged_decode_kernel<2>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, dec_smem_bytes(2));
+        r = cudaFuncSetAttribute(paged_decode_kernel<1, 2>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, dec_smem_bytes(1, 2));
+      if (r == cudaSuccess)
+        r = cudaFuncSetAttribute(paged_decode_kernel<2, 3>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, dec_smem_bytes(2, 3));
       return r;
     });
     if (e != cudaSuccess) return cuda_fail(e, "fi_paged_decode: cudaFuncSetAttribute");
   }
   dim3 grid((unsigned)max_splits, (unsigned)num_kv_heads, (unsigned)batch);
-  // At most one CTA per SM: two page groups per CTA (see paged_decode_kernel).
-  const bool two = max_splits * num_kv_heads * batch <= (int64_t)sm_count();
-  cudaError_t e =
-      two ? launch_pdl(paged_decode_kernel<2>, grid, dim3(dec_threads(2)), dec_smem_bytes(2), s,
-                       tmk, tmv, p)
-          : launch_pdl(paged_decode_kernel<1>, grid, dim3(dec_threads(1)), dec_smem_bytes(1), s,
-                       tmk, tmv, p);
+  // At most one CTA per SM: two page groups per CTA (see paged_decode_kernel). Two
+  // to four CTAs per SM: a 2-slot ring and three resident CTAs per SM, so the CTAs
+  // that have pages (splits past a sequence's end exit at once) fit one wave; measured
+  // on config 5 with one KV head (256 sequences, 512 CTAs): 58.7 vs 63.2 us, and
+  // within 1 % either way on the grids of config 3 and config 5 with 2-8 KV heads.
+  const int64_t ctas = max_splits * num_kv_heads * batch, sms = sm_count();
+  cudaError_t e;
+  if (ctas <= sms)
+    e = launch_pdl(paged_decode_kernel<2, 3>, grid, dim3(dec_threads(2)), dec_smem_bytes(2, 3), s,
+                   tmk, tmv, p);
+  else if (ctas <= 4 * sms)
+    e = launch_pdl(paged_decode_kernel<1, 2>, grid, dim3(dec_threads(1)), dec_smem_bytes(1, 2), s,
+                   tmk, tmv, p);
+  else
+    e = launch_pdl(paged_decode_kernel<1, 3>, grid, dim3(dec_threads(1)), dec_smem_bytes(1, 3), s,
+                   tmk, tmv, p);
   if (e != cudaSuccess) return cuda_fail(e, "fi_paged_decode: launch");
   if (max_splits > 1) {
     dim3 g2((unsigned)((num_q_heads + 3) / 4), (unsigned)batch);

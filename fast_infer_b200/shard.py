@@ -176,6 +176,11 @@ class PeerGather:
             device_errors(self._err, "peer gather")
         return self._buffers[buffer, :rows].view(*local.shape[:-1], self.world * self.row_elems)
 
+    def result(self, buffer: int, rows: int):
+        """This rank's buffer ``buffer`` as [rows, world * row_elems]: what the last
+        gather into it delivered (rank p's block at columns [p * row_elems, ...))."""
+        return self._buffers[buffer, :rows]
+
     def errors(self) -> int:
         """FI_DEVERR_* bits raised by any gather so far (synchronises the stream)."""
         return int(self._err.item())

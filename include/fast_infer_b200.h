@@ -4,10 +4,11 @@
  * Drop-in boundary for Fast_Infer's attention path. Every entry point takes raw
  * device pointers, element strides (int64, in elements, one per tensor dimension,
  * outermost first), shapes, a softmax scale and a CUDA stream (cudaStream_t passed
- * as void*). Nothing here allocates, synchronises the stream or keeps global state:
- * calls are asynchronous on `stream`, re-entrant, and every buffer belongs to the
- * caller (the peer-gather set-up calls at the end are the exception: they allocate
- * and map the shared regions once). Each call returns FI_OK or an FI_ERR_* code
+ * as void*). Nothing here allocates or synchronises the stream, and the only state
+ * kept between calls is per-device set-up (kernel attributes, SM counts), made once
+ * under a lock: calls are asynchronous on `stream`, re-entrant and thread-safe, and
+ * every buffer belongs to the caller (the peer-gather set-up calls at the end are
+ * the exception: they allocate and map the shared regions once). Each call returns FI_OK or an FI_ERR_* code
  * after validating its
  * arguments on the host; fi_last_error() then gives a one-line message
  * (thread-local).
@@ -124,7 +125,8 @@ size_t fi_paged_decode_workspace_size(int64_t batch, int64_t num_q_heads, int64_
  *               Sequences with 0 tokens produce zeros (kernels/attention.py:205-206).
  * workspace   : caller-owned device buffer of at least
  *               fi_paged_decode_workspace_size(...) bytes (may be NULL when that is 0).
- * pages_per_split: KV pages per split-KV partition; 0 = automatic.
+ * pages_per_split: KV pages per split-KV partition; 0 = automatic. Deterministic:
+ *               a call repeated on the same inputs gives the same bits.
  */
 int fi_paged_decode(const void* q, const void* k_cache, const void* v_cache, void* o,
                     const int32_t* block_table, const int32_t* context_lens, int64_t num_tokens,

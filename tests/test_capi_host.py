@@ -135,6 +135,7 @@ def test_automatic_split_rule():
     cases = [(64, 24, 8, 4096, 2),     # config 3: 32 pages per split, two splits at most
              (16, 24, 8, 1280, 1),     # the stack's decode step: unsplit
              (256, 24, 8, 4096, 2),    # config 5
+             (256, 3, 1, 4096, 2),     # config 5, one KV head per rank (8-GPU partition)
              (1, 24, 8, 8192, 9),      # one long sequence: 9 splits of 15 pages
              (2, 3, 1, 4096, 16)]      # one KV head: splits floored at 4 pages
     for batch, hq, hkv, ctx, nsplit in cases:

@@ -190,3 +190,55 @@ def test_extreme_magnitudes(cuda_device, device_checks, scale):
                           pages_per_split=4).cpu().numpy()
     assert np.isfinite(out).all()
     _ok(out, paged_attention_fp32(q, kc, vc, bt, lens))
+
+
+@pytest.mark.parametrize("batch,hq,hkv,lo,hi,zeros", [
+    (256, 3, 1, 1024, 4096, 0),    # config 5 with one KV head per rank (8-GPU partition)
+    (16, 24, 8, 1025, 1025, 0),    # the stack's decode step
+    (1, 24, 8, 8000, 8000, 0),     # one long sequence in many splits
+    (2, 6, 2, 1, 70, 0),           # a few short sequences
+    (40, 24, 8, 0, 300, 7),        # empty sequences among short ones
+    (1280, 24, 8, 1, 200, 0),      # a wide batch of short sequences
+    (33, 32, 4, 100, 2000, 3),     # GQA group of 8
+])
+def test_automatic_split_shapes(cuda_device, device_checks, batch, hq, hkv, lo, hi, zeros):
+    """The automatic split over grids from a handful of CTAs to many waves, with empty
+    sequences, one long sequence, the largest GQA group: against fp32, run twice for
+    identical bits, and against a fixed 32-page split within tolerance."""
+    from fast_infer_b200.kernels.attention import paged_attention
+    rng = np.random.default_rng(batch * 7 + hq + hi)
+    lens = rng.integers(lo, hi + 1, size=batch).astype(np.int32)
+    if zeros:
+        lens[rng.choice(batch, zeros, replace=False)] = 0
+    q, kc, vc, bt = _random_paged(rng, np.maximum(lens, 1), hq, hkv)
+    args = (_to(q, cuda_device), _to(kc, cuda_device), _to(vc, cuda_device),
+            _to(bt, cuda_device), 64, 0)
+    kw = dict(context_lens=_to(lens, cuda_device), max_context_len=int(lens.max()))
+    out = paged_attention(*args, **kw)
+    again = paged_attention(*args, **kw)
+    assert torch.equal(out, again)
+    o = out.cpu().numpy()
+    assert not o[lens == 0].any()
+    idx = np.arange(batch) if batch <= 64 else np.arange(0, batch, batch // 32)
+    _ok(o[idx], paged_attention_fp32(q[idx], kc, vc, bt[idx], lens[idx]), "vs fp32")
+    fixed = paged_attention(*args, pages_per_split=32, **kw).cpu().numpy()
+    _ok(o.astype(np.float32), fixed.astype(np.float32), "vs fixed split")
+
+
+def test_context_beyond_launch_bound(cuda_device):
+    """A context longer than max_context_len is truncated to the bound's pages and
+    reported as FI_DEVERR_CONTEXT_LEN."""
+    from fast_infer_b200._runtime import device_checks
+    from fast_infer_b200.kernels.attention import paged_attention
+    rng = np.random.default_rng(5)
+    lens = np.array([500, 200, 64], np.int32)
+    q, kc, vc, bt = _random_paged(rng, lens, 24, 8)
+    args = (_to(q, cuda_device), _to(kc, cuda_device), _to(vc, cuda_device),
+            _to(bt, cuda_device), 64, 0)
+    with device_checks(True):
+        with pytest.raises(RuntimeError, match="context"):
+            paged_attention(*args, context_lens=_to(lens, cuda_device), max_context_len=256)
+    out = paged_attention(*args, context_lens=_to(lens, cuda_device),
+                          max_context_len=256).cpu().numpy()
+    cut = np.minimum(lens, 256)
+    _ok(out, paged_attention_fp32(q, kc, vc, bt, cut))
