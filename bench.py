@@ -605,14 +605,16 @@ def run_stack(torch, dev, rank, world, dist, warmup=1):
     torch.cuda.synchronize()
     dec_ms = max_ms(e[0].elapsed_time(e[1]))
     finite = bool(torch.isfinite(h).all().item())
-    peer_errors = st._peer.errors() if st._peer is not None else 0
+    peer_errors = ((st._peer.errors() if st._peer is not None else 0) |
+                   (st._reduce.errors() if st._reduce is not None else 0))
     checks = stack_checks(torch, dev, rank, world, dist, st, prompt, use_graph, sync_all)
     return {
         "workload": "config 4: 28-layer attention stack (Llama-3.2-3B attention shapes, random "
                     "weights), B16, prefill 1024 then 256 decode steps, KV heads sharded over "
-                    f"{world} GPU(s), head outputs all-gathered per layer (decode: one "
-                    "peer-memory kernel over NVLink; prefill: NCCL); prefill = median of 3 "
-                    "timed passes",
+                    f"{world} GPU(s); decode: O projection sharded by head with the cross-rank "
+                    "sum over NVLink inside the GEMM (one kernel per layer); prefill: NCCL "
+                    "all-gather of head outputs, whole O projection per rank; prefill = median "
+                    "of 3 timed passes",
         "scaling": "strong",
         "prefill_ms": round(pf_ms, 3),
         "prefill_tokens_per_s": round(STACK_BATCH * STACK_PROMPT / (pf_ms * 1e-3), 1),
@@ -620,7 +622,7 @@ def run_stack(torch, dev, rank, world, dist, warmup=1):
         "decode_tokens_per_s": round(STACK_BATCH * STACK_STEPS / (dec_ms * 1e-3), 1),
         "cuda_graph": use_graph,
         "finite": finite,
-        "peer_gather_errors": peer_errors,
+        "peer_errors": peer_errors,
         **checks,
     }
 
@@ -631,9 +633,11 @@ STACK_CHECK_PROMPT, STACK_CHECK_STEPS = 256, 8
 def stack_checks(torch, dev, rank, world, dist, st, prompt, use_graph, sync_all):
     """Correctness of the sharded stack, outside the timed region (closes ``st``).
 
-    * gather_bitexact: after a CUDA-graph decode, every rank's peer-memory gather
-      buffer of every layer equals the NCCL all-gather of each rank's own block
-      (order of the head blocks, and no word of an older call).
+    * reduce_vs_nccl: after a CUDA-graph decode, one more call of the stack's
+      O-projection peer reduce (layer 0's weights, seeded inputs per rank) against an
+      NCCL all-reduce of the ranks' fp32 partials plus the residual (worst rank).
+    * gather_bitexact (decode_exchange "gather" only): every rank's peer-memory gather
+      buffer of every layer equals the NCCL all-gather of each rank's own block.
     * ranks_identical: every rank holds the same hidden state.
     * stack_vs_n1: rank 0 runs the same prompt and decode steps through an unsharded
       stack (one GPU, same seed) and compares the decode outputs. Tolerance: relative
@@ -645,8 +649,29 @@ def stack_checks(torch, dev, rank, world, dist, st, prompt, use_graph, sync_all)
     if world == 1:
         st.close()
         sync_all()
-        return {"gather_bitexact": None, "ranks_identical": None, "stack_vs_n1": None}
+        return {"reduce_vs_nccl": None, "gather_bitexact": None, "ranks_identical": None,
+                "stack_vs_n1": None}
     out_n = st.generate(prompt[:, :STACK_CHECK_PROMPT], STACK_CHECK_STEPS, use_graph=use_graph)
+    reduce_check = None
+    if st._reduce is not None:
+        w = st.layers[0]["wo_part"]
+        g = torch.Generator(device=dev)
+        g.manual_seed(50 + rank)
+        x = torch.randn(STACK_BATCH, w.shape[1], generator=g, device=dev).half()
+        g.manual_seed(51)  # the residual stream is the same on every rank
+        res = torch.randn(STACK_BATCH, w.shape[0], generator=g, device=dev).half()
+        out = torch.empty_like(res)
+        st._reduce.linear(x, w, res, out, 0)  # the graph's last call used buffer L-1
+        ref = x.float() @ w.float().t()
+        dist.all_reduce(ref)
+        ref += res.float()
+        max_abs, rel = _err(torch, out, ref)
+        scale = ref.abs().max().item()
+        max_abs, rel, scale = _reduce(torch, dev, dist, [max_abs, rel, scale], dist.ReduceOp.MAX)
+        reduce_check = {"max_abs": max_abs, "rel_l2": rel, "max_abs_ref": scale,
+                        "ok": rel <= TOL_REL_L2 and max_abs <= TOL_MAX_ABS * max(1.0, scale),
+                        "what": "O-projection peer reduce (16 x 3072, k = 3072 / N per rank) vs "
+                                "NCCL all-reduce of fp32 partials + residual, worst rank"}
     same = 1.0
     if st._peer is not None:
         w = st._peer.row_elems
@@ -682,7 +707,8 @@ def stack_checks(torch, dev, rank, world, dist, st, prompt, use_graph, sync_all)
         del one
         torch.cuda.empty_cache()
     sync_all()
-    return {"gather_bitexact": (gather_ok == 1.0) if had_peer else None,
+    return {"reduce_vs_nccl": reduce_check,
+            "gather_bitexact": (gather_ok == 1.0) if had_peer else None,
             "ranks_identical": ident == 1.0, "stack_vs_n1": vs}
 
 

@@ -83,6 +83,10 @@ SIGNATURES = {
     "fi_peer_free": (ctypes.c_int, [_vp]),
     "fi_peer_gather": (ctypes.c_int, [_vp, _i64, _i64, _i64, ctypes.POINTER(_vp), _i64, _i64, _i64,
                                       _i64, _i64, _vp, _vp]),
+    "fi_peer_reduce_bytes": (_sz, [_i64, _i64, _i64]),
+    "fi_small_gemm_peer_reduce": (ctypes.c_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64p,
+                                                 _i64p, _i64p, _i64p, ctypes.POINTER(_vp),
+                                                 _i64, _i64, _i64, _i64, _i64, _vp, _vp]),
 }
 
 _lock = threading.Lock()

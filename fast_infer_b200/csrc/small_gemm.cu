@@ -309,7 +309,27 @@ struct SsArgs {
   int nq, nkv;
   int64_t max_pos, tab_stride, num_blocks, block_size, max_blocks;
   int64_t qs[3], kcs[4], vcs[4], bts[2];
+  // kReduce epilogue (fi_small_gemm_peer_reduce): the item's partial sums go to every
+  // rank's landing area; the output is residual + the ranks' partials in rank order
+  uint8_t* peer[8];        // each rank's region as mapped here
+  int world, rank;
+  int64_t land_off;        // this call's landing buffer within a region
+  int64_t land_rank_bytes; // bytes of one source rank's slots within a buffer
+  uint32_t* epoch;         // this rank's call counter (local)
+  uint32_t* counter;       // CTA arrivals of the current call (local)
 };
+
+// kReduce landing slot of one item from one rank: 16 tokens x 16 outputs as fp16,
+// three per 8-byte word with the call's 16-bit epoch in the top half of the second
+// word (the flag travels inside the data: an 8-byte store reaches the peer whole).
+constexpr int kPrSlotWords = 88;  // ceil(256 / 3) = 86, padded
+
+__device__ __forceinline__ void st_word8(uint8_t* p, uint32_t lo, uint32_t hi) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(lo), "r"(hi) : "memory");
+}
+__device__ __forceinline__ void ld_word8(const uint8_t* p, uint32_t& lo, uint32_t& hi) {
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(lo), "=r"(hi) : "l"(p) : "memory");
+}
 
 // kS = 3 ring stages: two CTAs per SM; kS = 2: three (registers capped to fit).
 template <int NT, int kS>
@@ -318,7 +338,7 @@ __host__ __device__ constexpr size_t ss_smem_bytes() {
          (size_t)kSgWarps * 16 * 4 + 16 * 4;
 }
 
-template <int NT, bool kFold, bool kRope, int kSsStages>
+template <int NT, bool kFold, bool kRope, int kSsStages, bool kReduce = false>
 __global__ void __launch_bounds__(kSgThreads, kSsStages == 2 ? 3 : 2)
     small_gemm_stream_kernel(const __grid_constant__ CUtensorMap tm_w,
                              const __grid_constant__ CUtensorMap tm_x, const SsArgs a) {
@@ -384,6 +404,10 @@ __global__ void __launch_bounds__(kSgThreads, kSsStages == 2 ? 3 : 2)
 
   // ---------------------------------------------------------------- math warps
   grid_dep_wait();  // the residual may be the previous kernel's output
+  // kReduce: this call's epoch (the previous call's last CTA raised the counter
+  // before its grid completed; every CTA reads it before any CTA of this call can)
+  const uint32_t epoch = kReduce ? *a.epoch + 1 : 0;
+  bool give_up = kReduce && a.err && (*reinterpret_cast<volatile int*>(a.err) & FI_DEVERR_TIMEOUT);
   const int g = lane >> 2, t = lane & 3;
   const int arow = lane & 15, ahalf = lane >> 4;
   float acc[NT][4];
@@ -525,6 +549,58 @@ __global__ void __launch_bounds__(kSgThreads, kSsStages == 2 ? 3 : 2)
         dst[d0 * cs[3]] = ol;
         dst[d1 * cs[3]] = oh;
       }
+    } else if constexpr (kReduce) {
+      // Thread w < kWords owns values 3w..3w+2 of the item (value v = token v/16,
+      // output v%16): sends its word of this rank's partial to every rank, then sums
+      // every rank's word in rank order, adds the residual and stores.
+      constexpr int kVals = NT * 8 * kSgRows;
+      constexpr int kWords = (kVals + 2) / 3;
+      const int nbase = item * kSgRows;
+      if (tid < kWords) {
+        uint32_t hv[3];
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+          const int v = tid * 3 + j;
+          float sum = 0.f;
+          if (v < kVals) {
+#pragma unroll
+            for (int w = 0; w < kSgWarps; ++w) sum += red[w][v >> 4][v & 15];
+          }
+          hv[j] = __half_as_ushort(__float2half_rn(sum));
+        }
+        const uint32_t lo = hv[0] | (hv[1] << 16), hi = hv[2] | ((epoch & 0xFFFFu) << 16);
+        const int64_t off = a.land_off + a.rank * a.land_rank_bytes +
+                            ((int64_t)item * kPrSlotWords + tid) * 8;
+        for (int p = 0; p < a.world; ++p) st_word8(a.peer[p] + off, lo, hi);
+        float part[3] = {0.f, 0.f, 0.f};
+        const unsigned long long t0 = globaltimer_ns();
+        for (int p = 0; p < a.world; ++p) {
+          const uint8_t* src = a.peer[a.rank] + a.land_off + p * a.land_rank_bytes +
+                               ((int64_t)item * kPrSlotWords + tid) * 8;
+          uint32_t x, y;
+          ld_word8(src, x, y);
+          uint32_t spins = 0;
+          while ((y >> 16) != (epoch & 0xFFFFu) && !give_up) {
+            if ((++spins & 63u) == 0u && globaltimer_ns() - t0 > kWaitTimeoutNs) {
+              set_error(a.err, FI_DEVERR_TIMEOUT);
+              give_up = true;
+            }
+            ld_word8(src, x, y);
+          }
+          part[0] += __half2float(__ushort_as_half((unsigned short)(x & 0xFFFFu)));
+          part[1] += __half2float(__ushort_as_half((unsigned short)(x >> 16)));
+          part[2] += __half2float(__ushort_as_half((unsigned short)(y & 0xFFFFu)));
+        }
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+          const int v = tid * 3 + j, m = v >> 4, n = nbase + (v & 15);
+          if (v < kVals && m < a.M && n < a.N) {
+            float out = part[j];
+            if (a.res) out += __half2float(a.res[m * a.rs0 + n * a.rs1]);
+            a.c[m * a.cs0 + n * a.cs1] = __float2half_rn(out);
+          }
+        }
+      }
     } else {
       const int nbase = item * kSgRows;
       for (int i = tid; i < a.M * kSgRows; i += kSgWarps * 32) {
@@ -541,29 +617,38 @@ __global__ void __launch_bounds__(kSgThreads, kSsStages == 2 ? 3 : 2)
     }
     named_bar_sync(kSgBar, kSgWarps * 32);
   }
+  if constexpr (kReduce) {
+    // the last CTA of this call raises the epoch for the next call
+    if (tid == 0 && atomicAdd(a.counter, 1u) == gridDim.x - 1) {
+      atomicExch(a.counter, 0u);
+      *a.epoch = epoch;
+    }
+  }
 }
 
-template <int NT, bool kFold, bool kRope, int kS>
+template <int NT, bool kFold, bool kRope, int kS, bool kReduce = false>
 static int launch_small_gemm_stream_s(cudaStream_t st, const CUtensorMap& tw,
                                       const CUtensorMap& tx, const SsArgs& a) {
   constexpr size_t smem = ss_smem_bytes<NT, kS>();
   static DeviceOnce attr_once;
   {
     const cudaError_t e = attr_once.run([] {
-      return cudaFuncSetAttribute(small_gemm_stream_kernel<NT, kFold, kRope, kS>,
+      return cudaFuncSetAttribute(small_gemm_stream_kernel<NT, kFold, kRope, kS, kReduce>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     });
     if (e != cudaSuccess) return cuda_fail(e, "fi_small_gemm: cudaFuncSetAttribute");
   }
   int nb = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, small_gemm_stream_kernel<NT, kFold, kRope, kS>,
-                                                    kSgThreads, smem) != cudaSuccess || nb < 1)
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+          &nb, small_gemm_stream_kernel<NT, kFold, kRope, kS, kReduce>, kSgThreads, smem) !=
+          cudaSuccess ||
+      nb < 1)
     nb = 1;
   const int items = (a.N + kSgRows - 1) / kSgRows;
   int grid = nb * sm_count();
   if (grid > items) grid = items;
-  cudaError_t e = launch_pdl(small_gemm_stream_kernel<NT, kFold, kRope, kS>, dim3((unsigned)grid),
-                             dim3(kSgThreads), smem, st, tw, tx, a);
+  cudaError_t e = launch_pdl(small_gemm_stream_kernel<NT, kFold, kRope, kS, kReduce>,
+                             dim3((unsigned)grid), dim3(kSgThreads), smem, st, tw, tx, a);
   if (e != cudaSuccess) return cuda_fail(e, "fi_small_gemm launch");
   return FI_OK;
 }
@@ -805,4 +890,106 @@ extern "C" int fi_qkv_rope_kv_write(
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return batch <= 8 ? launch_small_gemm_stream<1, true, true>(st, tw, tx, a)
                     : launch_small_gemm_stream<2, true, true>(st, tw, tx, a);
+}
+
+// ---------------------------------------------------------------------------
+// O projection sharded by input rows across ranks, reduced over NVLink inside the
+// GEMM: c = residual + sum over ranks p (in rank order) of fp16(x_p @ w_p^T), where
+// every rank passes its own x_p [m, k] (its heads' attention output) and w_p [n, k]
+// (the matching columns of the projection). Each work item (16 outputs) stores its
+// partial into every rank's landing area and sums all ranks' partials for those
+// outputs, so the exchange costs no launch and no separate rendezvous; every rank
+// ends with the same bits in c.
+//
+// Region of each rank (fi_peer_alloc, shared with fi_peer_open):
+//   [landing: nbuf buffers x world source ranks x items x kPrSlotWords x 8 bytes]
+//   [local state: call counter, CTA arrival counter]
+
+namespace fi {
+static int64_t pr_land_rank_bytes(int64_t n) {
+  return ((n + kSgRows - 1) / kSgRows) * kPrSlotWords * 8;
+}
+}  // namespace fi
+
+extern "C" size_t fi_peer_reduce_bytes(int64_t nbuf, int64_t world, int64_t n) {
+  using namespace fi;
+  if (nbuf <= 0 || world <= 0 || world > 8 || n <= 0 || n > (1 << 24)) return 0;
+  return (size_t)(nbuf * world * pr_land_rank_bytes(n)) + 256;
+}
+
+extern "C" int fi_small_gemm_peer_reduce(const void* x, const void* w, void* c,
+                                         const void* residual, int64_t m, int64_t n, int64_t k,
+                                         const int64_t* x_strides, const int64_t* w_strides,
+                                         const int64_t* c_strides,
+                                         const int64_t* residual_strides, void* const* bases,
+                                         int64_t world, int64_t rank, int64_t buffer,
+                                         int64_t nbuf, int64_t flags, int32_t* error_flag,
+                                         void* stream) {
+  using namespace fi;
+  clear_error();
+  if (m < 0 || n <= 0 || n > (1 << 24) || k <= 0)
+    return fail(FI_ERR_INVALID_ARG, "fi_small_gemm_peer_reduce: bad sizes");
+  if (flags & ~(int64_t)FI_STATIC_WEIGHTS)
+    return fail(FI_ERR_INVALID_ARG, "fi_small_gemm_peer_reduce: unknown flags %lld",
+                (long long)flags);
+  if (world < 1 || world > 8 || rank < 0 || rank >= world)
+    return fail(FI_ERR_INVALID_ARG, "fi_small_gemm_peer_reduce: world %lld / rank %lld",
+                (long long)world, (long long)rank);
+  if (nbuf <= 0 || buffer < 0 || buffer >= nbuf)
+    return fail(FI_ERR_INVALID_ARG, "fi_small_gemm_peer_reduce: bad buffer index");
+  // A rank that has every partial of call k may send call k+1's while a slower rank
+  // still reads call k's landing area: consecutive calls need different buffers.
+  if (world > 1 && nbuf < 2)
+    return fail(FI_ERR_INVALID_ARG, "fi_small_gemm_peer_reduce: %lld ranks need at least 2 buffers",
+                (long long)world);
+  if (m > kSgMaxM)
+    return fail(FI_ERR_UNSUPPORTED, "fi_small_gemm_peer_reduce: M (%lld) > %d", (long long)m,
+                kSgMaxM);
+  if (k % kSgChunk != 0 || k > (1 << 20))
+    return fail(FI_ERR_UNSUPPORTED,
+                "fi_small_gemm_peer_reduce: K must be a multiple of 64 (and <= 2^20)");
+  if (!x || !w || !c || !x_strides || !w_strides || !c_strides || !bases ||
+      (residual && !residual_strides))
+    return fail(FI_ERR_INVALID_ARG, "fi_small_gemm_peer_reduce: null pointer argument");
+  if (x_strides[1] != 1 || x_strides[0] % 8 != 0 || !aligned16(x) || w_strides[1] != 1 ||
+      w_strides[0] % 8 != 0 || !aligned16(w))
+    return fail(FI_ERR_ALIGNMENT,
+                "fi_small_gemm_peer_reduce: x and w rows must be contiguous and 16-byte aligned");
+  SsArgs a;
+  memset(&a, 0, sizeof(a));
+  for (int p = 0; p < world; ++p) {
+    if (!bases[p] || !aligned16(bases[p]))
+      return fail(FI_ERR_INVALID_ARG, "fi_small_gemm_peer_reduce: region of rank %d missing", p);
+    a.peer[p] = static_cast<uint8_t*>(bases[p]);
+  }
+  if (m == 0) return FI_OK;  // no tokens: every rank skips the call alike
+  CUtensorMap tw, tx;
+  {
+    const int r = stream_maps(x, w, m, n, k, x_strides, w_strides, &tw, &tx);
+    if (r != FI_OK) return r;
+  }
+  a.res = static_cast<const __half*>(residual);
+  a.c = static_cast<__half*>(c);
+  a.err = error_flag;
+  a.M = (int)m;
+  a.N = (int)n;
+  a.K = (int)k;
+  a.rounds = (int)((k + kSgRoundK - 1) / kSgRoundK);
+  a.w_static = (flags & FI_STATIC_WEIGHTS) != 0;
+  a.cs0 = c_strides[0];
+  a.cs1 = c_strides[1];
+  if (residual) {
+    a.rs0 = residual_strides[0];
+    a.rs1 = residual_strides[1];
+  }
+  a.world = (int)world;
+  a.rank = (int)rank;
+  a.land_rank_bytes = pr_land_rank_bytes(n);
+  a.land_off = buffer * world * a.land_rank_bytes;
+  uint32_t* state = reinterpret_cast<uint32_t*>(a.peer[rank] + nbuf * world * a.land_rank_bytes);
+  a.epoch = state;
+  a.counter = state + 1;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return m <= 8 ? launch_small_gemm_stream_s<1, false, false, 3, true>(st, tw, tx, a)
+                : launch_small_gemm_stream_s<2, false, false, 3, true>(st, tw, tx, a);
 }

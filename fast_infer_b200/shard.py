@@ -100,6 +100,48 @@ class _DeviceArray:
                                          "data": (ptr, False), "version": 3}
 
 
+def _map_regions(nbytes: int, world: int, rank: int, group, device):
+    """Allocate this rank's peer region and map every other rank's (CUDA IPC handles
+    exchanged with ``all_gather_object``; collective). Returns (own pointer, pointers
+    opened here, a ctypes array of every rank's region as seen from this rank)."""
+    import ctypes
+    import torch
+    import torch.distributed as dist
+    from fast_infer_b200 import _lib
+    lib = _lib.load()
+    own = ctypes.c_void_p()
+    handle = (ctypes.c_uint8 * 64)()
+    with torch.cuda.device(device):
+        _lib.check(lib.fi_peer_alloc(nbytes, ctypes.byref(own), handle), "fi_peer_alloc")
+    handles = [None] * world
+    dist.all_gather_object(handles, bytes(handle), group=group)
+    opened, bases = [], []
+    with torch.cuda.device(device):
+        for p, hb in enumerate(handles):
+            if p == rank:
+                bases.append(own.value)
+                continue
+            ptr = ctypes.c_void_p()
+            hbuf = (ctypes.c_uint8 * 64).from_buffer_copy(hb)
+            _lib.check(lib.fi_peer_open(hbuf, ctypes.byref(ptr)), "fi_peer_open")
+            opened.append(ptr.value)
+            bases.append(ptr.value)
+    return own.value, opened, (ctypes.c_void_p * 8)(*bases, *([None] * (8 - world)))
+
+
+def _unmap_regions(lib, own, opened, device, group):
+    """Unmap the peers' regions, then free this rank's once every rank has unmapped
+    it (collective)."""
+    import torch
+    import torch.distributed as dist
+    torch.cuda.synchronize(device)
+    with torch.cuda.device(device):
+        for p in opened:
+            lib.fi_peer_close(p)
+        dist.barrier(group=group)
+        lib.fi_peer_free(own)
+
+
 class PeerGather:
     """``gather_heads`` for the decode step, over NVLink peer memory instead of NCCL.
 
@@ -117,7 +159,6 @@ class PeerGather:
     """
 
     def __init__(self, max_rows: int, row_elems: int, nbuf: int, group=None, device=None):
-        import ctypes
         import torch
         import torch.distributed as dist
         from fast_infer_b200 import _lib
@@ -131,28 +172,9 @@ class PeerGather:
         self.device = torch.device(device or "cuda")
         self.max_rows, self.row_elems, self.nbuf = max_rows, row_elems, nbuf
         self._lib = lib = _lib.load()
-        row_total = self.world * row_elems * 2
-        nbytes = lib.fi_peer_gather_bytes(nbuf, max_rows, row_total)
-        own = ctypes.c_void_p()
-        handle = (ctypes.c_uint8 * 64)()
-        with torch.cuda.device(self.device):
-            _lib.check(lib.fi_peer_alloc(nbytes, ctypes.byref(own), handle), "fi_peer_alloc")
-        self._own = own.value
-        handles = [None] * self.world
-        dist.all_gather_object(handles, bytes(handle), group=group)
-        self._opened = []
-        bases = []
-        with torch.cuda.device(self.device):
-            for p, hb in enumerate(handles):
-                if p == self.rank:
-                    bases.append(self._own)
-                    continue
-                ptr = ctypes.c_void_p()
-                hbuf = (ctypes.c_uint8 * 64).from_buffer_copy(hb)
-                _lib.check(lib.fi_peer_open(hbuf, ctypes.byref(ptr)), "fi_peer_open")
-                self._opened.append(ptr.value)
-                bases.append(ptr.value)
-        self._bases = (ctypes.c_void_p * 8)(*bases, *([None] * (8 - self.world)))
+        nbytes = lib.fi_peer_gather_bytes(nbuf, max_rows, self.world * row_elems * 2)
+        self._own, self._opened, self._bases = _map_regions(nbytes, self.world, self.rank, group,
+                                                            self.device)
         self._buffers = torch.as_tensor(
             _DeviceArray(self._own, (nbuf, max_rows, self.world * row_elems)), device=self.device)
         # persistent device error word of every gather (FI_DEVERR_TIMEOUT once a wait ran
@@ -188,16 +210,76 @@ class PeerGather:
     def close(self, group=None):
         """Unmap the peers' regions and free this rank's once every rank has unmapped
         it (collective: every rank calls it)."""
-        import torch
-        import torch.distributed as dist
         if self._own is None:
             return
-        torch.cuda.synchronize(self.device)
-        with torch.cuda.device(self.device):
-            for p in self._opened:
-                self._lib.fi_peer_close(p)
-            self._opened = []
-            self._buffers = None
-            dist.barrier(group=group)
-            self._lib.fi_peer_free(self._own)
-        self._own = None
+        self._buffers = None
+        _unmap_regions(self._lib, self._own, self._opened, self.device, group)
+        self._own, self._opened = None, []
+
+
+class PeerReduce:
+    """The O projection of a KV-head-sharded decode step with its cross-rank sum over
+    NVLink peer memory, in one kernel (``fi_small_gemm_peer_reduce``).
+
+    ``linear(x, w_part, residual, out, buffer)`` computes, on every rank,
+    out = residual + sum over ranks p (rank order) of fp16(x_p @ w_part_p^T): x_p
+    [rows, k] is rank p's heads' attention output, w_part_p [n, k] the projection's
+    input columns of those heads. Every rank ends with the same bits. Every rank must
+    make the same sequence of calls, consecutive calls using different buffers (more
+    than one rank needs ``nbuf >= 2``; the stack uses one buffer per layer). Construct
+    it on every rank at the same point (it runs collectives); call ``close`` before the
+    process group goes away.
+    """
+
+    def __init__(self, n: int, nbuf: int, group=None, device=None):
+        import torch
+        import torch.distributed as dist
+        from fast_infer_b200 import _lib
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("PeerReduce supports up to 8 ranks")
+        if self.world > 1 and nbuf < 2:
+            raise ValueError(f"PeerReduce over {self.world} ranks needs nbuf >= 2, got {nbuf}")
+        self.device = torch.device(device or "cuda")
+        self.n, self.nbuf = n, nbuf
+        self._lib = lib = _lib.load()
+        nbytes = lib.fi_peer_reduce_bytes(nbuf, self.world, n)
+        self._own, self._opened, self._bases = _map_regions(nbytes, self.world, self.rank, group,
+                                                            self.device)
+        # persistent device error word (FI_DEVERR_TIMEOUT once a wait ran out; later
+        # calls then skip their waits); read with ``errors()``
+        self._err = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def linear(self, x, w_part, residual, out, buffer: int, static_weight: bool = False):
+        import ctypes
+        from fast_infer_b200 import _lib
+        from fast_infer_b200._runtime import device_errors, error_word, stream_of
+        x2 = x.reshape(-1, x.shape[-1])
+        if x2.stride(-1) != 1 or x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
+            x2 = x2.contiguous()
+        o2 = out.view(-1, out.shape[-1])
+        r2 = residual.reshape(-1, residual.shape[-1]) if residual is not None else None
+        st = self._lib.fi_small_gemm_peer_reduce(
+            x2.data_ptr(), w_part.data_ptr(), o2.data_ptr(),
+            r2.data_ptr() if r2 is not None else None, x2.shape[0], w_part.shape[0],
+            x2.shape[1], _lib.strides(*x2.stride()), _lib.strides(*w_part.stride()),
+            _lib.strides(*o2.stride()), _lib.strides(*r2.stride()) if r2 is not None else None,
+            ctypes.cast(self._bases, ctypes.POINTER(ctypes.c_void_p)), self.world, self.rank,
+            buffer, self.nbuf, _lib.FI_STATIC_WEIGHTS if static_weight else 0,
+            self._err.data_ptr(), stream_of(self.device))
+        _lib.check(st, "peer reduce")
+        if error_word(self.device) is not None:  # device checks on: raise at once
+            device_errors(self._err, "peer reduce")
+        return out
+
+    def errors(self) -> int:
+        """FI_DEVERR_* bits raised by any call so far (synchronises the stream)."""
+        return int(self._err.item())
+
+    def close(self, group=None):
+        """Unmap the peers' regions and free this rank's (collective)."""
+        if self._own is None:
+            return
+        _unmap_regions(self._lib, self._own, self._opened, self.device, group)
+        self._own, self._opened = None, []

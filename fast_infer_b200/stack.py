@@ -9,9 +9,12 @@ of each decoder layer is not part of this harness (it is not on the attention pa
 
 Sharding by KV head (``fast_infer_b200.shard``): rank r of N holds the QKV weight
 columns of its KV heads and their query heads, and a KV cache with Hkv/N heads;
-attention needs no exchange; the per-rank attention outputs [tokens, Hq/N * D] are
-all-gathered (NCCL) into [tokens, Hq * D] before the O projection, which every rank
-applies in full (replicated), so every rank carries the whole hidden state.
+attention needs no exchange. Every rank carries the whole hidden state. In the
+decode step each rank multiplies its heads' attention output [tokens, Hq/N * D] by
+the matching input columns of the O projection, and the ranks' partial outputs are
+summed over NVLink inside that GEMM (``PeerReduce``, one kernel per layer; every rank
+gets the same bits). Prefill all-gathers the per-rank attention outputs (NCCL) into
+[tokens, Hq * D] and applies the whole O projection on every rank.
 
 Decode is autoregressive in hidden space: the stack's output for token t is the
 input of token t+1 (there is no embedding or sampler in an attention-only stack).
@@ -28,8 +31,6 @@ below restate the reference's RoPE and RMSNorm in PyTorch for tests.
 
 from __future__ import annotations
 
-import os
-
 from typing import Callable, Optional
 
 import torch
@@ -39,7 +40,7 @@ from fast_infer_b200.kernels.attention import flash_attention, paged_attention
 from fast_infer_b200.kernels.matmul import fold_rms_weight, fp16_linear
 from fast_infer_b200.kernels.rms_norm import rms_norm
 from fast_infer_b200.kv_cache import KVCache, permute_rope_rows, qkv_rope_store, rope_and_store
-from fast_infer_b200.shard import HeadShard, PeerGather, gather_heads, head_shard
+from fast_infer_b200.shard import HeadShard, PeerGather, PeerReduce, gather_heads, head_shard
 
 
 def precompute_freqs(head_dim: int, max_seq_len: int, theta: float, device) -> tuple:
@@ -72,7 +73,15 @@ class AttentionStack:
                  num_kv_heads: int = 8, head_dim: int = 128, rope_theta: float = 500000.0,
                  rms_eps: float = 1e-5, batch: int = 16, max_seq_len: int = 1280,
                  rank: int = 0, world: int = 1, device=None, seed: int = 0,
-                 gather: Optional[Callable[[torch.Tensor], torch.Tensor]] = None):
+                 gather: Optional[Callable[[torch.Tensor], torch.Tensor]] = None,
+                 decode_exchange: str = "reduce"):
+        """``decode_exchange`` (multi-rank decode): "reduce" = O projection sharded by
+        head with the cross-rank sum in the GEMM (``PeerReduce``); "gather" = head
+        outputs gathered over peer memory (``PeerGather``), whole O projection on every
+        rank; "nccl" = the same with an NCCL all-gather. A custom ``gather`` callable
+        or fewer than two layers use the gather path with that callable / NCCL."""
+        if decode_exchange not in ("reduce", "gather", "nccl"):
+            raise ValueError(f"decode_exchange must be reduce, gather or nccl: {decode_exchange}")
         self.device = torch.device(device or "cuda")
         self.L, self.hidden, self.D = num_layers, hidden, head_dim
         self.hq, self.hkv = num_q_heads, num_kv_heads
@@ -81,11 +90,13 @@ class AttentionStack:
         self.shard: HeadShard = head_shard(rank, world, num_q_heads, num_kv_heads)
         self.world = world
         self.gather = gather if gather is not None else gather_heads
-        # decode-step gather over NVLink peer memory (set up with the decode state on
-        # multi-rank CUDA runs that use the default gather; FI_P2P_GATHER=0 keeps NCCL)
+        # decode-step exchange over NVLink peer memory, set up with the decode state on
+        # multi-rank runs that use the default gather (one buffer per layer, so two
+        # consecutive calls never share one: at least two layers)
         self._peer = None
-        self._peer_wanted = (gather is None and world > 1 and num_layers >= 2 and
-                             os.environ.get("FI_P2P_GATHER", "1") != "0")
+        self._reduce = None
+        peer_ok = gather is None and world > 1 and num_layers >= 2
+        self._exchange = decode_exchange if peer_ok else "nccl"
         g = torch.Generator(device=self.device)
         g.manual_seed(seed)
         dev = self.device
@@ -106,10 +117,14 @@ class AttentionStack:
             wqkv_t = wqkv.t().half().contiguous()
             # decode: norm weight folded in, rows permuted so each 16-row tile holds
             # its rotary pairs (one launch for norm + QKV + RoPE + slot writes)
+            wo_t = wo.t().half().contiguous()
             self.layers.append(dict(norm=norm.half(), wqkv_t=wqkv_t,
                                     wqkv_rope=permute_rope_rows(
                                         fold_rms_weight(wqkv_t, norm.half())),
-                                    wo_t=wo.t().half().contiguous()))
+                                    wo_t=wo_t,
+                                    # the O projection's input columns of this rank's heads
+                                    wo_part=wo_t[:, q_cols].contiguous()
+                                    if self._exchange == "reduce" else None))
         self.cos, self.sin = precompute_freqs(head_dim, max_seq_len, rope_theta, self.device)
         pages_per_seq = (max_seq_len + 63) // 64
         self.cache = KVCache(num_layers, sh.num_kv_heads, head_dim, max_seq_len, 64, self.device,
@@ -126,7 +141,7 @@ class AttentionStack:
         if self.world == 1:
             return o
         if layer is not None and self._peer is not None:
-            return self._peer.gather(o, layer % self._peer.nbuf)  # one buffer per layer
+            return self._peer.gather(o, layer)  # one buffer per layer
         return self.gather(o)
 
     @staticmethod
@@ -177,8 +192,10 @@ class AttentionStack:
             self._ws = torch.empty(max(need, 1), dtype=torch.uint8, device=self.device)
             self._h_in = torch.zeros(B, 1, self.hidden, dtype=torch.float16, device=self.device)
             self._graph = None
-            if self._peer_wanted and self._peer is None:
-                self._peer = PeerGather(B, self.shard.num_q_heads * self.D, max(self.L, 2),
+            if self._exchange == "reduce" and self._reduce is None:
+                self._reduce = PeerReduce(self.hidden, self.L, device=self.device)
+            elif self._exchange == "gather" and self._peer is None:
+                self._peer = PeerGather(B, self.shard.num_q_heads * self.D, self.L,
                                         device=self.device)
 
     def _decode_body(self):
@@ -196,6 +213,11 @@ class AttentionStack:
             o = paged_attention(q[:, 0], self.cache.k[li], self.cache.v[li],
                                 self.cache.block_table, 64, 0, context_lens=self._dev_ctx,
                                 max_context_len=span, workspace=self._ws)
+            if self._reduce is not None:  # h += sum over ranks of o_r @ Wo_r, one kernel
+                hv = h.view(B, self.hidden)
+                self._reduce.linear(o.view(B, nq * D), w["wo_part"], hv, hv, li,
+                                    static_weight=True)
+                continue
             o = self._gather(o.reshape(B, 1, nq * D), li)
             fp16_linear(o, w["wo_t"], residual=h, out=h, static_weight=True)  # h += o @ Wo
         self._dev_ctx.add_(1)
@@ -261,12 +283,15 @@ class AttentionStack:
         self._graph = None
 
     def close(self):
-        """Release the decode graph and the peer-memory gather buffers (collective on
+        """Release the decode graph and the peer-memory buffers (collective on
         multi-rank runs: every rank calls it before the process group goes away)."""
         self.release_graph()
         if self._peer is not None:
             self._peer.close()
             self._peer = None
+        if self._reduce is not None:
+            self._reduce.close()
+            self._reduce = None
 
     def forward(self, h: torch.Tensor) -> torch.Tensor:
         """Reference-style entry (model.py:50-160): S > 1 or the first call = prefill,

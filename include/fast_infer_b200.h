@@ -383,6 +383,36 @@ int fi_peer_gather(const void* src, int64_t rows, int64_t row_bytes, int64_t src
                    void* const* bases, int64_t world, int64_t rank, int64_t buffer, int64_t nbuf,
                    int64_t max_rows, int32_t* error_flag, void* stream);
 
+/*
+ * O projection of a stack sharded by KV head, reduced across ranks over NVLink peer
+ * memory inside the GEMM (no separate gather, no replicated projection).
+ *
+ * Replaces, for the decode step of a KV-head-sharded stack, the all-gather of the
+ * per-rank head outputs plus the replicated O projection and residual add
+ * (model.py:123-135 with the heads split over GPUs): every rank multiplies only its
+ * own heads' output by the matching input columns of the projection.
+ *
+ * c[i, :] = residual[i, :] + sum over ranks p, in rank order, of fp16(x_p[i, :] @ w_p^T)
+ *   x_p : [m, k] fp16 on rank p, m <= 16 (x_strides: 2 entries, innermost 1)
+ *   w_p : [n, k] fp16 on rank p, the projection's input columns of rank p's heads
+ *   c, residual : [m, n] fp16 (may be the same buffer); identical bits on every rank.
+ * k a multiple of 64. Set-up as for fi_peer_gather: fi_peer_alloc a region of
+ * fi_peer_reduce_bytes(nbuf, world, n) bytes on every rank, fi_peer_open the others'.
+ * Each call uses landing buffer `buffer`; consecutive calls must use different
+ * buffers (world > 1 needs nbuf >= 2, FI_ERR_INVALID_ARG otherwise). Calls are
+ * counted on the device, so a CUDA graph replays correctly; every rank makes the same
+ * sequence of calls. A rank waits for the others' partials (bounded: 2 s, then
+ * FI_DEVERR_TIMEOUT in error_flag; later calls given a word holding it do not wait).
+ * flags: FI_STATIC_WEIGHTS as for fi_small_gemm.
+ */
+size_t fi_peer_reduce_bytes(int64_t nbuf, int64_t world, int64_t n);
+int fi_small_gemm_peer_reduce(const void* x, const void* w, void* c, const void* residual,
+                              int64_t m, int64_t n, int64_t k, const int64_t* x_strides,
+                              const int64_t* w_strides, const int64_t* c_strides,
+                              const int64_t* residual_strides, void* const* bases, int64_t world,
+                              int64_t rank, int64_t buffer, int64_t nbuf, int64_t flags,
+                              int32_t* error_flag, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

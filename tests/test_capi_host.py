@@ -275,6 +275,35 @@ def test_peer_gather_host_checks():
     assert lib.fi_peer_free(None) == _lib.FI_OK
 
 
+def test_peer_reduce_host_checks():
+    """fi_small_gemm_peer_reduce's region size (one 704-byte slot per 16 outputs, per
+    source rank and buffer, plus the local state) and the argument checks that answer
+    before any device work, including two or more ranks with one buffer."""
+    lib = _lib.load()
+    assert lib.fi_peer_reduce_bytes(0, 2, 3072) == 0
+    assert lib.fi_peer_reduce_bytes(2, 9, 3072) == 0
+    assert lib.fi_peer_reduce_bytes(2, 2, 0) == 0
+    for nbuf, world, n in ((28, 8, 3072), (2, 2, 100), (1, 1, 16)):
+        items = -(-n // 16)
+        assert lib.fi_peer_reduce_bytes(nbuf, world, n) == nbuf * world * items * 88 * 8 + 256
+    s2 = _lib.strides(64, 1)
+    bases = (ctypes.c_void_p * 2)(16, 16)
+    pb = ctypes.cast(bases, ctypes.POINTER(ctypes.c_void_p))
+
+    def call(x=16, w=16, c=16, m=4, n=64, k=64, world=2, rank=0, buffer=0, nbuf=2, flags=0, b=pb):
+        return lib.fi_small_gemm_peer_reduce(x, w, c, None, m, n, k, s2, s2, s2, None, b, world,
+                                             rank, buffer, nbuf, flags, None, None)
+    bad = _lib.FI_ERR_INVALID_ARG
+    assert call(world=0) == bad and call(world=9) == bad and call(rank=2) == bad
+    assert call(buffer=2) == bad and call(nbuf=0) == bad
+    assert call(nbuf=1) == bad and "at least 2 buffers" in lib.fi_last_error().decode()
+    assert call(flags=4) == bad
+    assert call(m=17) == _lib.FI_ERR_UNSUPPORTED
+    assert call(k=100) == _lib.FI_ERR_UNSUPPORTED
+    assert call(x=None) == bad and call(b=None) == bad
+    assert call(x=8) == _lib.FI_ERR_ALIGNMENT
+
+
 def test_norm_rope_varlen_host_checks():
     """fi_rms_norm, fi_rope_kv_write and fi_prefill_fwd_varlen reject bad sizes,
     unsupported shapes and null pointers before any device work, and treat empty

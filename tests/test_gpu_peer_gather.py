@@ -1,8 +1,8 @@
 """Decode-step head gather over NVLink peer memory (fi_peer_gather), one rank per GPU
 on every GPU of the box (2 to 8): the gathered rows equal an NCCL all-gather bit for bit over many calls with
 rotating buffers and ragged row counts, and when replayed from a CUDA graph; the
-KV-head-sharded stack decodes the same bits with the peer gather as with NCCL, on
-every rank; no gather reports a time-out. Skipped on a box with fewer than two GPUs."""
+KV-head-sharded stack (decode_exchange="gather") decodes the same bits with the peer
+gather as with NCCL, on every rank; no gather reports a time-out. Skipped on a box with fewer than two GPUs."""
 
 import datetime
 import os
@@ -73,18 +73,17 @@ def _worker(rank, world, port, out_dir):
         pg.close()
 
         results = {}
-        for mode in ("1", "0"):
-            os.environ["FI_P2P_GATHER"] = mode
+        for mode in ("gather", "nccl"):
             st = AttentionStack(num_layers=3, batch=4, max_seq_len=256, rank=rank, world=world,
-                                device=dev, seed=7)
+                                device=dev, seed=7, decode_exchange=mode)
             gp = torch.Generator(device=dev)
             gp.manual_seed(8)
             prompt = (torch.randn(4, 64, 3072, generator=gp, device=dev) * 0.5).half()
             results[mode] = st.generate(prompt, steps=6, use_graph=True).cpu()
             checks[f"peer_used_{mode}"] = st._peer is not None
             st.close()
-        checks["stack_same_bits"] = torch.equal(results["1"], results["0"])
-        torch.save({"checks": checks, "out": results["1"]}, Path(out_dir) / f"r{rank}.pt")
+        checks["stack_same_bits"] = torch.equal(results["gather"], results["nccl"])
+        torch.save({"checks": checks, "out": results["gather"]}, Path(out_dir) / f"r{rank}.pt")
     finally:
         dist.destroy_process_group()
 
@@ -160,7 +159,7 @@ def test_peer_gather_all_gpus(tmp_path):
     res = [torch.load(tmp_path / f"r{r}.pt") for r in range(world)]
     for r in res:
         assert r["checks"] == {"eager": True, "graph": True, "no_timeout": True,
-                               "peer_used_1": True, "peer_used_0": False,
+                               "peer_used_gather": True, "peer_used_nccl": False,
                                "stack_same_bits": True}, r["checks"]
     for r in res[1:]:
         assert torch.equal(res[0]["out"], r["out"])
