@@ -192,7 +192,12 @@ __device__ __forceinline__ void decode_page(uint32_t st, int row_base, int lane,
 // could wait on a slot two phases ahead, and the parity test would report the
 // previous phase as the one it wants.
 // kSt = ring slots per group: 3 with two CTAs per SM, 2 with three (kGrp = 1 only).
-template <int kGrp, int kSt>
+// kCl > 1 (small grids): the kCl splits of a (sequence, KV head) form one thread-block
+// cluster; each CTA leaves its merged (max, sum, acc) in its own shared memory and
+// CTA 0 of the cluster reads the others' through distributed shared memory, merges
+// and writes the output: no workspace and no combine launch. Every CTA of a cluster,
+// with pages or not, reaches both cluster barriers.
+template <int kGrp, int kSt, int kCl>
 __global__ void __launch_bounds__(dec_threads(kGrp), kGrp == 1 ? (kSt == 2 ? 3 : 2) : 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const DecodeParams p) {
@@ -213,17 +218,21 @@ __global__ void __launch_bounds__(dec_threads(kGrp), kGrp == 1 ? (kSt == 2 ? 3 :
   const int npages = seq_pages(p, b, ctx, split == 0 && threadIdx.x == 0 && kvh == 0);
   const int pg0 = split * p.pps;
 
-  if (npages == 0) {  // empty sequence: output zeros (kernels/attention.py:205-206)
-    if (split == 0 && threadIdx.x < p.group * (kD / 8)) {
-      const int h = kvh * p.group + threadIdx.x / (kD / 8);
-      const int d0 = (threadIdx.x % (kD / 8)) * 8;
-      __half* orow = p.o + b * p.os[0] + h * p.os[1];
-      for (int d = 0; d < 8; ++d) orow[(d0 + d) * p.os[2]] = __float2half(0.f);
+  if constexpr (kCl == 1) {
+    if (npages == 0) {  // empty sequence: output zeros (kernels/attention.py:205-206)
+      if (split == 0 && threadIdx.x < p.group * (kD / 8)) {
+        const int h = kvh * p.group + threadIdx.x / (kD / 8);
+        const int d0 = (threadIdx.x % (kD / 8)) * 8;
+        __half* orow = p.o + b * p.os[0] + h * p.os[1];
+        for (int d = 0; d < 8; ++d) orow[(d0 + d) * p.os[2]] = __float2half(0.f);
+      }
+      return;
     }
-    return;
+    if (pg0 >= npages) return;
   }
-  if (pg0 >= npages) return;
-  const int n = min(npages - pg0, p.pps);
+  // pages of this CTA (cluster CTAs past the sequence's end have none; an empty
+  // sequence merges to zeros)
+  const int n = pg0 < npages ? min(npages - pg0, p.pps) : 0;
   const int nsplits = (npages + p.pps - 1) / p.pps;
 
   if (threadIdx.x == 0) {
@@ -268,6 +277,10 @@ __global__ void __launch_bounds__(dec_threads(kGrp), kGrp == 1 ? (kSt == 2 ? 3 :
       }
     }
     __syncthreads();  // pairs with the consumers' barrier before the merge
+    if constexpr (kCl > 1) {  // the cluster merge's two barriers
+      cluster_sync_all();
+      cluster_sync_all();
+    }
     return;
   }
 
@@ -329,7 +342,16 @@ __global__ void __launch_bounds__(dec_threads(kGrp), kGrp == 1 ? (kSt == 2 ? 3 :
     }
   }
   named_bar_sync(1, kCW * 32);
-  if (aborted || threadIdx.x >= kDecWarps * 32) return;
+  // cluster merge buffers, past the warps' (the ring is free): [8 heads][128] + (M, L)
+  float* s_cl = s_l + kCW * 8;
+  float2* s_clml = reinterpret_cast<float2*>(s_cl + 8 * kD);
+  if ((kCl == 1 && aborted) || threadIdx.x >= kDecWarps * 32) {
+    if constexpr (kCl > 1) {
+      cluster_sync_all();
+      cluster_sync_all();
+    }
+    return;
+  }
   {
     const int t = threadIdx.x;            // 0..127
     const int h = t >> 4;                 // head slot 0..7
@@ -352,7 +374,12 @@ __global__ void __launch_bounds__(dec_threads(kGrp), kGrp == 1 ? (kSt == 2 ? 3 :
         }
       }
       const int hq = kvh * p.group + h;
-      if (nsplits == 1) {
+      if (kCl > 1) {  // leave this split's state for the cluster's CTA 0
+        float4* dst = reinterpret_cast<float4*>(s_cl + h * kD + d0);
+        dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+        dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+        if ((t & 15) == 0) s_clml[h] = make_float2(M, L);
+      } else if (nsplits == 1) {
         const float inv = (L > 0.f) ? 1.f / L : 0.f;
         __half* orow = p.o + b * p.os[0] + hq * p.os[1];
         if (p.os[2] == 1 && ((reinterpret_cast<uintptr_t>(orow + d0) & 15) == 0)) {
@@ -373,6 +400,54 @@ __global__ void __launch_bounds__(dec_threads(kGrp), kGrp == 1 ? (kSt == 2 ? 3 :
         if ((t & 15) == 0) p.ws_ml[slot] = make_float2(M, L);
       }
     }
+  }
+  if constexpr (kCl > 1) {
+    cluster_sync_all();  // every split's state is in its CTA's shared memory
+    const int t = threadIdx.x, h = t >> 4, d0 = (t & 15) * 8;
+    if (split == 0 && h < p.group) {
+      float Ms[kCl], Ls[kCl];
+      float M = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < kCl; ++r) {
+        const float2 ml = ld_cluster_f2(cluster_map(smem_u32(s_clml + h), r));
+        Ms[r] = ml.x;
+        Ls[r] = ml.y;
+        M = fmaxf(M, ml.x);
+      }
+      float L = 0.f, o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = 0.f;
+      if (M != -INFINITY) {
+#pragma unroll
+        for (int r = 0; r < kCl; ++r) {
+          const float wt = fast_exp2(Ms[r] - M);
+          L += Ls[r] * wt;
+          const uint32_t src = cluster_map(smem_u32(s_cl + h * kD + d0), r);
+          const float4 a = ld_cluster_f4(src), c = ld_cluster_f4(src + 16);
+          o[0] += a.x * wt;
+          o[1] += a.y * wt;
+          o[2] += a.z * wt;
+          o[3] += a.w * wt;
+          o[4] += c.x * wt;
+          o[5] += c.y * wt;
+          o[6] += c.z * wt;
+          o[7] += c.w * wt;
+        }
+      }
+      const float inv = (L > 0.f) ? 1.f / L : 0.f;
+      __half* orow = p.o + b * p.os[0] + (kvh * p.group + h) * p.os[1];
+      if (p.os[2] == 1 && ((reinterpret_cast<uintptr_t>(orow + d0) & 15) == 0)) {
+        uint4 pk;
+        pk.x = pack_half2(o[0] * inv, o[1] * inv);
+        pk.y = pack_half2(o[2] * inv, o[3] * inv);
+        pk.z = pack_half2(o[4] * inv, o[5] * inv);
+        pk.w = pack_half2(o[6] * inv, o[7] * inv);
+        *reinterpret_cast<uint4*>(orow + d0) = pk;
+      } else {
+        for (int e = 0; e < 8; ++e) orow[(d0 + e) * p.os[2]] = __float2half(o[e] * inv);
+      }
+    }
+    cluster_sync_all();  // CTA 0 has read every CTA's shared memory
   }
 }
 
@@ -440,6 +515,28 @@ static int64_t max_pages_of(int64_t max_context_len) {
   return max_context_len <= 0 ? 1 : (max_context_len + kPage - 1) / kPage;
 }
 
+#ifndef FI_DEC_CLUSTER_MAX
+#define FI_DEC_CLUSTER_MAX 8
+#endif
+#ifndef FI_DEC_CLUSTER_MIN_PAGES
+#define FI_DEC_CLUSTER_MIN_PAGES 4
+#endif
+// Automatic split of a small grid: when one CTA per (sequence, KV head) would leave
+// most SMs idle, the pages of each are split over a thread-block cluster of 2, 4 or 8
+// CTAs (about one CTA per SM in all; at least FI_DEC_CLUSTER_MIN_PAGES pages per CTA)
+// that merge in shared memory. Returns 1 when a cluster does not apply (explicit
+// split, large grids, or more than kMaxPagesPerSplit pages per CTA).
+static int choose_cluster(int64_t batch, int64_t hkv, int64_t max_pages, int64_t requested) {
+  if (requested > 0) return 1;
+  const int64_t units = batch * hkv > 0 ? batch * hkv : 1;
+  int64_t cs = (int64_t)sm_count() / units;
+  if (cs > FI_DEC_CLUSTER_MAX) cs = FI_DEC_CLUSTER_MAX;
+  if (cs > max_pages / FI_DEC_CLUSTER_MIN_PAGES) cs = max_pages / FI_DEC_CLUSTER_MIN_PAGES;
+  cs = cs >= 8 ? 8 : cs >= 4 ? 4 : cs >= 2 ? 2 : 1;
+  if (cs > 1 && (max_pages + cs - 1) / cs > kMaxPagesPerSplit) return 1;
+  return (int)cs;
+}
+
 }  // namespace fi
 
 extern "C" size_t fi_paged_decode_workspace_size(int64_t batch, int64_t num_q_heads,
@@ -451,6 +548,7 @@ extern "C" size_t fi_paged_decode_workspace_size(int64_t batch, int64_t num_q_he
       block_size != kPage)
     return 0;
   const int64_t mp = max_pages_of(max_context_len);
+  if (choose_cluster(batch, num_kv_heads, mp, pages_per_split) > 1) return 0;
   const int pps = choose_pps(batch, num_kv_heads, mp, pages_per_split);
   const int64_t max_splits = (mp + pps - 1) / pps;
   if (max_splits <= 1) return 0;
@@ -499,8 +597,10 @@ extern "C" int fi_paged_decode(const void* q, const void* k_cache, const void* v
     return fail(FI_ERR_UNSUPPORTED, "fi_paged_decode: context too long");
 
   const int64_t mp = max_pages_of(max_context_len);
-  const int pps = choose_pps(batch, num_kv_heads, mp, pages_per_split);
-  const int64_t max_splits = (mp + pps - 1) / pps;
+  const int cluster = choose_cluster(batch, num_kv_heads, mp, pages_per_split);
+  const int pps = cluster > 1 ? (int)((mp + cluster - 1) / cluster)
+                              : choose_pps(batch, num_kv_heads, mp, pages_per_split);
+  const int64_t max_splits = cluster > 1 ? cluster : (mp + pps - 1) / pps;
   const size_t need = fi_paged_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim,
                                                      max_context_len, block_size, pages_per_split);
   if (need > 0 && (!workspace || workspace_bytes < need))
@@ -557,14 +657,23 @@ extern "C" int fi_paged_decode(const void* q, const void* k_cache, const void* v
   static DeviceOnce attr_once;
   {
     const cudaError_t e = attr_once.run([] {
-      cudaError_t r = cudaFuncSetAttribute(paged_decode_kernel<1, 3>,
+      cudaError_t r = cudaFuncSetAttribute(paged_decode_kernel<1, 3, 1>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            dec_smem_bytes(1, 3));
       if (r == cudaSuccess)
-        r = cudaFuncSetAttribute(paged_decode_kernel<1, 2>,
+        r = cudaFuncSetAttribute(paged_decode_kernel<1, 2, 1>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, dec_smem_bytes(1, 2));
       if (r == cudaSuccess)
-        r = cudaFuncSetAttribute(paged_decode_kernel<2, 3>,
+        r = cudaFuncSetAttribute(paged_decode_kernel<2, 3, 1>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, dec_smem_bytes(2, 3));
+      if (r == cudaSuccess)
+        r = cudaFuncSetAttribute(paged_decode_kernel<2, 3, 2>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, dec_smem_bytes(2, 3));
+      if (r == cudaSuccess)
+        r = cudaFuncSetAttribute(paged_decode_kernel<2, 3, 4>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, dec_smem_bytes(2, 3));
+      if (r == cudaSuccess)
+        r = cudaFuncSetAttribute(paged_decode_kernel<2, 3, 8>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, dec_smem_bytes(2, 3));
       return r;
     });
@@ -578,14 +687,23 @@ extern "C" int fi_paged_decode(const void* q, const void* k_cache, const void* v
   // within 1 % either way on the grids of config 3 and config 5 with 2-8 KV heads.
   const int64_t ctas = max_splits * num_kv_heads * batch, sms = sm_count();
   cudaError_t e;
+  if (cluster > 1) {  // at most one CTA per SM, merged in shared memory: no combine launch
+    const dim3 blk(dec_threads(2));
+    const size_t sm = dec_smem_bytes(2, 3);
+    e = cluster == 2   ? launch_pdl_cluster(paged_decode_kernel<2, 3, 2>, grid, blk, sm, s, 2, tmk, tmv, p)
+        : cluster == 4 ? launch_pdl_cluster(paged_decode_kernel<2, 3, 4>, grid, blk, sm, s, 4, tmk, tmv, p)
+                       : launch_pdl_cluster(paged_decode_kernel<2, 3, 8>, grid, blk, sm, s, 8, tmk, tmv, p);
+    if (e != cudaSuccess) return cuda_fail(e, "fi_paged_decode: cluster launch");
+    return FI_OK;
+  }
   if (ctas <= sms)
-    e = launch_pdl(paged_decode_kernel<2, 3>, grid, dim3(dec_threads(2)), dec_smem_bytes(2, 3), s,
+    e = launch_pdl(paged_decode_kernel<2, 3, 1>, grid, dim3(dec_threads(2)), dec_smem_bytes(2, 3), s,
                    tmk, tmv, p);
   else if (ctas <= 4 * sms)
-    e = launch_pdl(paged_decode_kernel<1, 2>, grid, dim3(dec_threads(1)), dec_smem_bytes(1, 2), s,
+    e = launch_pdl(paged_decode_kernel<1, 2, 1>, grid, dim3(dec_threads(1)), dec_smem_bytes(1, 2), s,
                    tmk, tmv, p);
   else
-    e = launch_pdl(paged_decode_kernel<1, 3>, grid, dim3(dec_threads(1)), dec_smem_bytes(1, 3), s,
+    e = launch_pdl(paged_decode_kernel<1, 3, 1>, grid, dim3(dec_threads(1)), dec_smem_bytes(1, 3), s,
                    tmk, tmv, p);
   if (e != cudaSuccess) return cuda_fail(e, "fi_paged_decode: launch");
   if (max_splits > 1) {

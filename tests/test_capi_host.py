@@ -115,7 +115,10 @@ def test_decode_validation_and_workspace_size():
 
 
 def test_automatic_split_rule():
-    """The automatic split-KV choice, read back through the workspace it needs: about
+    """The automatic split-KV choice, read back through the workspace it needs. Grids
+    that would leave most SMs idle (at least two SMs per sequence x KV head) split each
+    over a thread-block cluster of 2, 4 or 8 CTAs (4 to 32 pages per CTA) that merge
+    in shared memory: no workspace. Otherwise about
     SMs / (2 x sequences x KV heads) splits per sequence, 4 to 32 pages each, and 32
     pages per split once that is one split (148 SMs: a B200, and the count the library
     assumes with no device)."""
@@ -127,6 +130,10 @@ def test_automatic_split_rule():
 
     def expect(batch, hq, hkv, max_ctx, sms=148):
         pages = -(-max_ctx // 64)
+        cs = min(sms // (batch * hkv), 8, pages // 4)
+        cs = 8 if cs >= 8 else 4 if cs >= 4 else 2 if cs >= 2 else 1
+        if cs > 1 and -(-pages // cs) <= 32:
+            return 0  # cluster merge in shared memory
         splits = sms // (2 * batch * hkv)
         pps = 32 if splits <= 1 else min(32, max(4, -(-pages // splits)))
         n = -(-pages // pps)
@@ -134,10 +141,13 @@ def test_automatic_split_rule():
 
     cases = [(64, 24, 8, 4096, 2),     # config 3: 32 pages per split, two splits at most
              (16, 24, 8, 1280, 1),     # the stack's decode step: unsplit
+             (16, 6, 2, 1280, 1),      # its 4-GPU share: clusters of 4 CTAs
              (256, 24, 8, 4096, 2),    # config 5
              (256, 3, 1, 4096, 2),     # config 5, one KV head per rank (8-GPU partition)
-             (1, 24, 8, 8192, 9),      # one long sequence: 9 splits of 15 pages
-             (2, 3, 1, 4096, 16)]      # one KV head: splits floored at 4 pages
+             (1, 24, 8, 8192, 1),      # one long sequence: clusters of 8, 16 pages each
+             (1, 24, 8, 32768, 16),    # too long for a cluster: 16 splits of 32 pages
+             (2, 3, 1, 4096, 1),       # one KV head: clusters of 8
+             (2, 3, 1, 500, 1)]        # 8 pages: clusters of 2 (4 pages per CTA)
     for batch, hq, hkv, ctx, nsplit in cases:
         ws = lib.fi_paged_decode_workspace_size(batch, hq, hkv, 128, ctx, 64, 0)
         assert ws == expect(batch, hq, hkv, ctx), (batch, hq, hkv, ctx)
