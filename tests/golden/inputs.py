@@ -124,3 +124,44 @@ def rms_inputs(rows: int, hidden: int):
         x[0] = (x[0].astype(np.float32) * 40.0).astype(np.float16)
     w = (1.0 + 0.1 * rng.standard_normal(size=(hidden,), dtype=np.float32)).astype(np.float16)
     return x, w
+
+
+# Reference model forward (model.py:50-160) with 2 layers of the Llama-3.2-3B shape
+# (hidden 3072, 24/8 heads, intermediate 8192) and a small vocabulary: a 62-token
+# prompt for 2 sequences, then 4 decode tokens (positions 62..65; the 65th token
+# starts a new page). The pool (max_seq_len 512) has 8 pages shared by the batch.
+MODEL = dict(layers=2, vocab=512, hidden=3072, intermediate=8192, heads=24, kv_heads=8,
+             head_dim=128, batch=2, prompt=62, decode_steps=4, max_seq_len=512)
+
+
+def model_weights():
+    """Seeded fp16 weights (numpy): embedding N(0,1) (tied LM head), norm weights
+    1 + 0.1 N(0,1), linear weights [out, in] N(0, 0.02) per layer."""
+    c = MODEL
+    rng = np.random.default_rng(61)
+    H, I, V = c["hidden"], c["intermediate"], c["vocab"]
+    kv = c["kv_heads"] * c["head_dim"]
+
+    def lin(n, k):
+        return (rng.standard_normal((n, k), dtype=np.float32) * 0.02).astype(np.float16)
+
+    def norm():
+        return (1.0 + 0.1 * rng.standard_normal(H, dtype=np.float32)).astype(np.float16)
+
+    embed = randn_f16(rng, (V, H))
+    layers = []
+    for _ in range(c["layers"]):
+        layers.append(dict(input_layernorm=norm(), post_attention_layernorm=norm(),
+                           q_proj=lin(H, H), k_proj=lin(kv, H), v_proj=lin(kv, H),
+                           o_proj=lin(H, H), gate_proj=lin(I, H), up_proj=lin(I, H),
+                           down_proj=lin(H, I)))
+    return dict(embed=embed, layers=layers, norm=norm())
+
+
+def model_token_ids():
+    """Prompt ids [batch, prompt] and the decode steps' ids [steps, batch, 1]."""
+    c = MODEL
+    rng = np.random.default_rng(62)
+    prompt = rng.integers(0, c["vocab"], size=(c["batch"], c["prompt"])).astype(np.int64)
+    steps = rng.integers(0, c["vocab"], size=(c["decode_steps"], c["batch"], 1)).astype(np.int64)
+    return prompt, steps

@@ -23,6 +23,14 @@ Fixtures:
                         cos/sin rows model.py:74-75 feeds it.
 * ``rms_norm.npz``      the reference's ``rms_norm`` Triton kernel (kernels/rms_norm.py)
                         on the ``RMS_CASES`` shapes.
+* ``model_forward.npz`` the reference's whole ``LlamaForCausalLM.forward`` (model.py:50-160,
+                        INT4 memory mode, 2 layers of the Llama-3.2-3B shape, vocabulary
+                        512): a 62-token prefill of 2 sequences and 4 decode tokens (the
+                        last starts a new page). Per forward and layer it records the
+                        attention inputs model.py passes (q after RoPE, k/v as stored), the
+                        attention outputs, the ``num_tokens`` given to paged attention, and
+                        after each forward the block table, free list, pool digests and
+                        logits.
 * ``int4.npz``          the reference's ``quantize_int4_groupwise`` and
                         ``dequantize_int4`` (loader.py), ``_dequant_storage`` and the
                         fused ``int4_matmul`` Triton kernel (kernels/matmul.py) on the
@@ -75,7 +83,7 @@ def digest(a: np.ndarray) -> str:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
-    ap.add_argument("--only", choices=["attention", "int4", "rms_norm"], default=None,
+    ap.add_argument("--only", choices=["attention", "int4", "rms_norm", "model"], default=None,
                     help="regenerate one group of fixtures (default: all)")
     args = ap.parse_args()
     ref_attn, ref_kv, ref_model, ref_rope = _import_reference(args.reference)
@@ -87,6 +95,8 @@ def main():
         _int4_fixtures(T)
     if args.only in (None, "rms_norm"):
         _rms_fixtures(T)
+    if args.only in (None, "model"):
+        _model_fixtures(ref_model, T)
     print("golden fixtures written to", HERE)
 
 
@@ -191,6 +201,82 @@ def _rms_fixtures(T):
         x, w = rms_inputs(rows, hidden)
         out[f"out_{rows}x{hidden}"] = ref_rms.rms_norm(T(x), T(w), 1e-5).numpy()
     np.savez_compressed(HERE / "rms_norm.npz", **out)
+
+
+def _model_fixtures(ref_model, T):
+    """The reference model's forward with its attention, slot writes and KV cache
+    recorded at the call sites model.py:113,117,120,123-130."""
+    import torch
+    from fast_infer.config import LlamaConfig  # type: ignore
+    from fast_infer.loader import quantize_int4_groupwise  # type: ignore
+    from tests.golden.inputs import MODEL, model_token_ids, model_weights
+    c = MODEL
+    cfg = LlamaConfig(num_hidden_layers=c["layers"], vocab_size=c["vocab"],
+                      max_seq_len=c["max_seq_len"])
+    w = model_weights()
+    q4 = lambda a: quantize_int4_groupwise(T(a))  # noqa: E731
+    layers = []
+    for lw in w["layers"]:
+        layers.append({
+            "input_layernorm": T(lw["input_layernorm"]),
+            "post_attention_layernorm": T(lw["post_attention_layernorm"]),
+            "self_attn": {n: q4(lw[n]) for n in ("q_proj", "k_proj", "v_proj", "o_proj")},
+            "mlp": {n: q4(lw[n]) for n in ("gate_proj", "up_proj", "down_proj")},
+        })
+    embed = T(w["embed"])
+    weights = {"embed_tokens": embed, "layers": layers, "norm": T(w["norm"]), "lm_head": embed}
+    model = ref_model.LlamaForCausalLM(cfg, weights, device=torch.device("cpu"),
+                                       memory_efficient=True)
+
+    rec = {}
+    call = {"i": 0, "layer": 0}
+    orig_fa, orig_pa = ref_model.flash_attention, ref_model.paged_attention
+    orig_pf, orig_dec = model._store_kv_prefill, model._store_kv_decode
+
+    def key(name):
+        return f"f{call['i']}_l{call['layer']}_{name}"
+
+    def fa(q, k, v, sm_scale=None):
+        o = orig_fa(q, k, v, sm_scale)
+        rec[key("q")] = q.transpose(1, 2).contiguous().numpy()   # [B, S, Hq, D]
+        rec[key("o")] = o.transpose(1, 2).contiguous().numpy()
+        return o
+
+    def pa(q, k_cache, v_cache, block_table, block_size, num_tokens, sm_scale=None):
+        o = orig_pa(q, k_cache, v_cache, block_table, block_size, num_tokens, sm_scale)
+        rec[key("q")] = q.contiguous().numpy()                    # [B, Hq, D]
+        rec[key("o")] = o.numpy()
+        rec[key("num_tokens")] = np.int64(num_tokens)
+        call["layer"] += 1
+        return o
+
+    def store_pf(layer_idx, k, v):
+        rec[key("k")], rec[key("v")] = k.contiguous().numpy(), v.contiguous().numpy()
+        orig_pf(layer_idx, k, v)
+        call["layer"] += 1
+
+    def store_dec(layer_idx, k, v):
+        rec[key("k")], rec[key("v")] = k.contiguous().numpy(), v.contiguous().numpy()
+        orig_dec(layer_idx, k, v)
+
+    ref_model.flash_attention, ref_model.paged_attention = fa, pa
+    model._store_kv_prefill, model._store_kv_decode = store_pf, store_dec
+    prompt, steps = model_token_ids()
+    try:
+        inputs = [prompt] + [steps[t] for t in range(steps.shape[0])]
+        for i, ids in enumerate(inputs):
+            call["i"], call["layer"] = i, 0
+            logits = model.forward(T(ids))
+            kv = model.kv_cache
+            rec[f"f{i}_logits"] = logits.numpy()
+            rec[f"f{i}_block_table"] = kv.block_table.numpy().copy()
+            rec[f"f{i}_free_blocks"] = np.array(kv.free_blocks, np.int64)
+            rec[f"f{i}_num_tokens"] = np.int64(kv.num_tokens)
+            rec[f"f{i}_k_sha"] = digest(kv.k.numpy())
+            rec[f"f{i}_v_sha"] = digest(kv.v.numpy())
+    finally:
+        ref_model.flash_attention, ref_model.paged_attention = orig_fa, orig_pa
+    np.savez_compressed(HERE / "model_forward.npz", **rec)
 
 
 def _int4_fixtures(T):

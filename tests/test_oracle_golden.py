@@ -142,3 +142,39 @@ def test_rope_oracle_bit_identical_to_reference():
     cos, _ = rope_tables(128, 4096)
     # fp32 cos of arguments up to ~300 rad: implementations differ by ~1e-5
     assert np.allclose(cos[ROPE_DECODE_POS], g["cos_fp32_row300"], atol=1e-4)
+
+
+def test_model_call_sequence_bit_identical_to_reference():
+    """The reference model's whole forward (tests/golden/model_forward.npz: 2 layers,
+    a 62-token prefill of 2 sequences, 4 decode tokens, the last starting a new page),
+    replayed call by call through the oracle with the inputs the reference's own calls
+    got: every attention output, block table, free list, num_tokens and pool digest of
+    the reference's run, bit for bit."""
+    from tests.golden.inputs import MODEL
+    c = MODEL
+    g = np.load(GOLDEN / "model_forward.npz")
+    cache = KVCacheOracle(c["layers"], c["kv_heads"], c["head_dim"], c["max_seq_len"], 64)
+    cache.grow_batch(c["batch"])
+    token_count = 0
+    for i in range(1 + c["decode_steps"]):
+        token_count = c["prompt"] if i == 0 else token_count + 1
+        for layer in range(c["layers"]):
+            key = f"f{i}_l{layer}_"
+            q, k, v = g[key + "q"], g[key + "k"], g[key + "v"]
+            if i == 0:  # model.py:104-117: BHSD views, K/V expanded for the kernel
+                G = c["heads"] // c["kv_heads"]
+                out = flash_attention_blockwise(
+                    q.transpose(0, 2, 1, 3), np.repeat(k.transpose(0, 2, 1, 3), G, axis=1),
+                    np.repeat(v.transpose(0, 2, 1, 3), G, axis=1)).transpose(0, 2, 1, 3)
+                store_kv_prefill(cache, layer, k, v)
+            else:  # model.py:118-131
+                store_kv_decode(cache, layer, k, v, token_count)
+                assert cache.num_tokens == int(g[key + "num_tokens"])
+                out = paged_attention_blockwise(q, cache.k[layer], cache.v[layer],
+                                                cache.block_table, 64,
+                                                num_tokens=cache.num_tokens)
+            assert np.array_equal(out, g[key + "o"]), key
+        assert np.array_equal(cache.block_table, g[f"f{i}_block_table"]), i
+        assert cache.free_blocks == g[f"f{i}_free_blocks"].tolist(), i
+        assert cache.num_tokens == int(g[f"f{i}_num_tokens"]), i
+        assert _sha(cache.k) == str(g[f"f{i}_k_sha"]) and _sha(cache.v) == str(g[f"f{i}_v_sha"]), i
