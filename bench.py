@@ -552,8 +552,10 @@ STACK_LAYERS, STACK_BATCH, STACK_PROMPT, STACK_STEPS = 28, 16, 1024, 256
 def run_stack(torch, dev, rank, world, dist, warmup=1):
     """Config 4: 28-layer attention stack (hidden 3072, 24/8 heads, RoPE 5e5, random
     N(0,0.02) fp16 weights), batch 16, prefill 1024 tokens then 256 decode steps,
-    KV heads sharded over the ranks (all-gather of head outputs before the
-    replicated O projection). Returns prefill / decode tokens/s of the whole job."""
+    KV heads sharded over the ranks (decode: O projection sharded by head, summed over
+    NVLink in the GEMM; prefill: residual stream split by token, all-to-all of head
+    outputs, O projection on each rank's tokens). Returns prefill / decode tokens/s of
+    the whole job."""
     from fast_infer_b200.stack import AttentionStack
     st = AttentionStack(num_layers=STACK_LAYERS, batch=STACK_BATCH,
                         max_seq_len=STACK_PROMPT + STACK_STEPS, rank=rank, world=world,
@@ -612,9 +614,10 @@ def run_stack(torch, dev, rank, world, dist, warmup=1):
         "workload": "config 4: 28-layer attention stack (Llama-3.2-3B attention shapes, random "
                     "weights), B16, prefill 1024 then 256 decode steps, KV heads sharded over "
                     f"{world} GPU(s); decode: O projection sharded by head with the cross-rank "
-                    "sum over NVLink inside the GEMM (one kernel per layer); prefill: NCCL "
-                    "all-gather of head outputs, whole O projection per rank; prefill = median "
-                    "of 3 timed passes",
+                    "sum over NVLink inside the GEMM (one kernel per layer); prefill: "
+                    "residual stream split by token over the ranks, NCCL all-gather of the "
+                    "normalised rows for QKV and all-to-all of the head outputs for the O "
+                    "projection of each rank's tokens; prefill = median of 3 timed passes",
         "scaling": "strong",
         "prefill_ms": round(pf_ms, 3),
         "prefill_tokens_per_s": round(STACK_BATCH * STACK_PROMPT / (pf_ms * 1e-3), 1),
@@ -643,14 +646,16 @@ def stack_checks(torch, dev, rank, world, dist, st, prompt, use_graph, sync_all)
       stack (one GPU, same seed) and compares the decode outputs. Tolerance: relative
       L2 <= 1e-3 and max-abs <= 2e-3 x max|output| (the max-abs
       scaled to the hidden state's magnitude, which grows over 28 residual layers).
-    At N = 1 only the stack itself ran; the three entries are null."""
+    * prefill_vs_n1: the same for the prefill's output (every token of the prompt).
+    At N = 1 only the stack itself ran; the entries are null."""
     from fast_infer_b200.shard import gather_heads
     from fast_infer_b200.stack import AttentionStack
     if world == 1:
         st.close()
         sync_all()
         return {"reduce_vs_nccl": None, "gather_bitexact": None, "ranks_identical": None,
-                "stack_vs_n1": None}
+                "stack_vs_n1": None, "prefill_vs_n1": None}
+    pf_n = st.prefill(prompt[:, :STACK_CHECK_PROMPT]).clone()
     out_n = st.generate(prompt[:, :STACK_CHECK_PROMPT], STACK_CHECK_STEPS, use_graph=use_graph)
     reduce_check = None
     if st._reduce is not None:
@@ -689,11 +694,19 @@ def stack_checks(torch, dev, rank, world, dist, st, prompt, use_graph, sync_all)
     st.close()
     del st
     torch.cuda.empty_cache()
-    vs = None
+    vs = pvs = None
     if rank == 0:
         one = AttentionStack(num_layers=STACK_LAYERS, batch=STACK_BATCH,
                              max_seq_len=STACK_PROMPT + STACK_STEPS, rank=0, world=1,
                              device=dev, seed=4)
+        pf_1 = one.prefill(prompt[:, :STACK_CHECK_PROMPT])
+        max_abs, rel = _err(torch, pf_n, pf_1)
+        scale = pf_1.abs().max().item()
+        pvs = {"max_abs": max_abs, "rel_l2": rel, "max_abs_ref": scale,
+               "ok": rel <= TOL_REL_L2 and max_abs <= TOL_MAX_ABS * max(1.0, scale),
+               "what": f"prefill output, every token of a {STACK_CHECK_PROMPT}-token prompt "
+                       f"(B{STACK_BATCH}, 28 layers), {world}-GPU sharded stack vs one GPU"}
+        del pf_1
         out_1 = one.generate(prompt[:, :STACK_CHECK_PROMPT], STACK_CHECK_STEPS,
                              use_graph=use_graph)
         max_abs, rel = _err(torch, out_n, out_1)
@@ -709,7 +722,7 @@ def stack_checks(torch, dev, rank, world, dist, st, prompt, use_graph, sync_all)
     sync_all()
     return {"reduce_vs_nccl": reduce_check,
             "gather_bitexact": (gather_ok == 1.0) if had_peer else None,
-            "ranks_identical": ident == 1.0, "stack_vs_n1": vs}
+            "ranks_identical": ident == 1.0, "stack_vs_n1": vs, "prefill_vs_n1": pvs}
 
 
 def int4_weight_bytes(n, k):

@@ -9,12 +9,14 @@ with no collective on the data path, one process per GPU:
   rank keeps a KVCache with Hkv/N heads and the full (replicated) block table;
 * by sequence — rank r owns a contiguous slice of the batch with all heads.
 
-The only collective is ``gather_heads``: where a caller needs the attention output
-whole (the O projection of a tensor-parallel-free layer), the per-rank
-[tokens, heads_r*D] outputs are all-gathered (NCCL over NVLink on B200; gloo in the
-CPU tests) and reassembled in head order. ``PeerGather`` does the same for the
-decode step in one kernel of our own: each rank stores its rows straight into every
-rank's buffer over NVLink (CUDA IPC mappings) and waits on per-call flags.
+Collectives for callers that need more than attention (NCCL over NVLink on B200; gloo
+in the CPU tests): ``gather_heads`` all-gathers the per-rank [tokens, heads_r*D]
+outputs and reassembles them in head order; ``heads_to_tokens`` (an all-to-all) hands
+each rank every head of its own block of tokens instead, and ``gather_rows``
+all-gathers row blocks — the pair a token-split prefill uses. ``PeerGather`` does the
+head gather for the decode step in one kernel of our own: each rank stores its rows
+straight into every rank's buffer over NVLink (CUDA IPC mappings) and waits on
+per-call flags; ``PeerReduce`` sums per-rank partial projections the same way.
 """
 
 from __future__ import annotations
@@ -90,6 +92,53 @@ def gather_heads(local, group=None, head_dim_axis: int = -1):
     parts = [torch.empty_like(local) for _ in range(world)]
     dist.all_gather(parts, local, group=group)
     return torch.cat(parts, dim=head_dim_axis)
+
+
+def token_block(rank: int, world: int, tokens: int) -> tuple[int, int]:
+    """Rows [start, end) of the token block a rank owns when a [tokens, ...] tensor is
+    split evenly by rows (``tokens`` a multiple of ``world``)."""
+    if tokens % world != 0:
+        raise ValueError(f"{tokens} tokens do not split evenly over {world} ranks")
+    per = tokens // world
+    return rank * per, (rank + 1) * per
+
+
+def gather_rows(local, group=None):
+    """All-gather equal row blocks: [T / world, ...] of every rank -> [T, ...] with rank
+    r's block at rows [r*T/world, (r+1)*T/world) (one collective)."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    if world == 1:
+        return local
+    local = local.contiguous()
+    out = torch.empty((world * local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype,
+                      device=local.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, local, group=group)
+    else:
+        dist.all_gather(list(out.chunk(world)), local, group=group)
+    return out
+
+
+def heads_to_tokens(local, group=None):
+    """Switch a [T, heads_r * D] tensor (this rank's heads, every token) to
+    [T / world, world * heads_r * D] (every head in head order, this rank's token block
+    of ``token_block``): one all-to-all of equal blocks, then one copy into head order.
+    Each rank sends and receives (world - 1) / world of its block — an all-gather of the
+    same outputs moves world times more."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    if world == 1:
+        return local
+    T, cols = local.shape
+    if T % world != 0:
+        raise ValueError(f"{T} tokens do not split evenly over {world} ranks")
+    local = local.contiguous()
+    recv = torch.empty_like(local)  # block j = rank j's heads of this rank's tokens
+    dist.all_to_all_single(recv, local, group=group)
+    return recv.view(world, T // world, cols).transpose(0, 1).reshape(T // world, world * cols)
 
 
 class _DeviceArray:

@@ -13,8 +13,9 @@ attention needs no exchange. Every rank carries the whole hidden state. In the
 decode step each rank multiplies its heads' attention output [tokens, Hq/N * D] by
 the matching input columns of the O projection, and the ranks' partial outputs are
 summed over NVLink inside that GEMM (``PeerReduce``, one kernel per layer; every rank
-gets the same bits). Prefill all-gathers the per-rank attention outputs (NCCL) into
-[tokens, Hq * D] and applies the whole O projection on every rank.
+gets the same bits). Prefill keeps the residual stream split by token: the normalised
+rows are all-gathered for the QKV projection, and an all-to-all hands each rank every
+head of its own rows for the O projection (NCCL; ``prefill``).
 
 Decode is autoregressive in hidden space: the stack's output for token t is the
 input of token t+1 (there is no embedding or sampler in an attention-only stack).
@@ -40,7 +41,8 @@ from fast_infer_b200.kernels.attention import flash_attention, paged_attention
 from fast_infer_b200.kernels.matmul import fold_rms_weight, fp16_linear
 from fast_infer_b200.kernels.rms_norm import rms_norm
 from fast_infer_b200.kv_cache import KVCache, permute_rope_rows, qkv_rope_store, rope_and_store
-from fast_infer_b200.shard import HeadShard, PeerGather, PeerReduce, gather_heads, head_shard
+from fast_infer_b200.shard import (HeadShard, PeerGather, PeerReduce, gather_heads, gather_rows,
+                                   head_shard, heads_to_tokens, token_block)
 
 
 def precompute_freqs(head_dim: int, max_seq_len: int, theta: float, device) -> tuple:
@@ -74,14 +76,20 @@ class AttentionStack:
                  rms_eps: float = 1e-5, batch: int = 16, max_seq_len: int = 1280,
                  rank: int = 0, world: int = 1, device=None, seed: int = 0,
                  gather: Optional[Callable[[torch.Tensor], torch.Tensor]] = None,
-                 decode_exchange: str = "reduce"):
+                 decode_exchange: str = "reduce", prefill_exchange: str = "tokens"):
         """``decode_exchange`` (multi-rank decode): "reduce" = O projection sharded by
         head with the cross-rank sum in the GEMM (``PeerReduce``); "gather" = head
         outputs gathered over peer memory (``PeerGather``), whole O projection on every
         rank; "nccl" = the same with an NCCL all-gather. A custom ``gather`` callable
-        or fewer than two layers use the gather path with that callable / NCCL."""
+        or fewer than two layers use the gather path with that callable / NCCL.
+        ``prefill_exchange`` (multi-rank prefill, see ``prefill``): "tokens" = residual
+        stream split by token, heads switched to tokens by an all-to-all; "gather" =
+        head outputs all-gathered, whole O projection on every rank (also used with a
+        custom ``gather`` callable, or when B*S does not split evenly)."""
         if decode_exchange not in ("reduce", "gather", "nccl"):
             raise ValueError(f"decode_exchange must be reduce, gather or nccl: {decode_exchange}")
+        if prefill_exchange not in ("tokens", "gather"):
+            raise ValueError(f"prefill_exchange must be tokens or gather: {prefill_exchange}")
         self.device = torch.device(device or "cuda")
         self.L, self.hidden, self.D = num_layers, hidden, head_dim
         self.hq, self.hkv = num_q_heads, num_kv_heads
@@ -97,6 +105,7 @@ class AttentionStack:
         self._reduce = None
         peer_ok = gather is None and world > 1 and num_layers >= 2
         self._exchange = decode_exchange if peer_ok else "nccl"
+        self._prefill_exchange = prefill_exchange if gather is None else "gather"
         g = torch.Generator(device=self.device)
         g.manual_seed(seed)
         dev = self.device
@@ -156,7 +165,17 @@ class AttentionStack:
     def prefill(self, h: torch.Tensor) -> torch.Tensor:
         """Prompt pass (reference model.py:67-69, 101-117): h [B, S, hidden] fp16.
         Per layer: projection, then one fused RoPE + KV slot-write launch, then the
-        causal prefill kernel on rotated q / k and the v columns of the projection."""
+        causal prefill kernel on rotated q / k and the v columns of the projection.
+
+        Several ranks with ``prefill_exchange="tokens"`` (the default): the residual
+        stream is kept split by token (rank r owns rows ``token_block(r)`` of the
+        flattened [B*S] tokens). Each layer normalises its own rows, all-gathers them
+        for the QKV projection of its heads, and after attention switches its heads'
+        outputs to every head of its own rows (``heads_to_tokens``: an all-to-all of
+        1/N of the outputs instead of an all-gather of all of them), so the O
+        projection and the residual add run on 1/N of the tokens. The full hidden
+        state is gathered once at the end. ``"gather"``: the head outputs are
+        all-gathered and every rank runs the whole O projection."""
         B, S, _ = h.shape
         self.reset()
         D, nq, nkv = self.D, self.shard.num_q_heads, self.shard.num_kv_heads
@@ -165,16 +184,42 @@ class AttentionStack:
             self.cache._ensure_blocks(b, need)
         self.cache.num_tokens = S
         k_rot = torch.empty(B, S, nkv, D, dtype=torch.float16, device=self.device)
-        h = h.contiguous().clone()  # the residual stream is updated in place below
+        if self.world > 1 and self._prefill_exchange == "tokens" and (B * S) % self.world == 0:
+            h = self._prefill_token_split(h, k_rot)
+        else:
+            h = h.contiguous().clone()  # the residual stream is updated in place below
+            for li, w in enumerate(self.layers):
+                qkv = self._qkv(w, h)
+                q_rot = rope_and_store(self.cache, li, qkv, nq, self.cos, self.sin, 0,
+                                       k_out=k_rot)
+                v = qkv[..., (nq + nkv) * D:].view(B, S, nkv, D)
+                o = flash_attention(q_rot.transpose(1, 2), k_rot.transpose(1, 2),
+                                    v.transpose(1, 2))
+                o = self._gather(o.transpose(1, 2).reshape(B, S, nq * D))
+                self._residual(h, o, w["wo_t"])
+        self.token_count = S
+        return h
+
+    def _prefill_token_split(self, h: torch.Tensor, k_rot: torch.Tensor) -> torch.Tensor:
+        """Layers of ``prefill`` with the residual stream split by token over the ranks
+        (see ``prefill``); returns the full [B, S, hidden] output on every rank."""
+        B, S, hid = h.shape
+        D, nq, nkv = self.D, self.shard.num_q_heads, self.shard.num_kv_heads
+        T = B * S
+        t0, t1 = token_block(self.shard.rank, self.world, T)
+        # this rank's rows of the stream, a copy: it is updated in place below (a row
+        # slice of a contiguous tensor is itself contiguous, so .contiguous() would alias
+        # the caller's h)
+        h_rows = h.reshape(T, hid)[t0:t1].clone()
         for li, w in enumerate(self.layers):
-            qkv = self._qkv(w, h)
+            x = gather_rows(rms_norm(h_rows, w["norm"], self.eps))  # [T, hidden]
+            qkv = (x @ w["wqkv_t"].t()).view(B, S, -1)
             q_rot = rope_and_store(self.cache, li, qkv, nq, self.cos, self.sin, 0, k_out=k_rot)
             v = qkv[..., (nq + nkv) * D:].view(B, S, nkv, D)
             o = flash_attention(q_rot.transpose(1, 2), k_rot.transpose(1, 2), v.transpose(1, 2))
-            o = self._gather(o.transpose(1, 2).reshape(B, S, nq * D))
-            self._residual(h, o, w["wo_t"])
-        self.token_count = S
-        return h
+            o_rows = heads_to_tokens(o.transpose(1, 2).reshape(T, nq * D))  # [T/N, Hq*D]
+            h_rows.addmm_(o_rows, w["wo_t"].t())  # h += o @ Wo on this rank's rows
+        return gather_rows(h_rows).view(B, S, hid)
 
     # ------------------------------------------------------------------- decode
     def _decode_state(self):

@@ -203,6 +203,15 @@ def _worker(rank, world, port, out_dir):
             checks[f"stack_errors_{mode}"] = st._reduce.errors() if st._reduce else 0
             st.close()
         checks["stack_close_to_nccl"] = _rel(results["reduce"], results["nccl"]) < 1e-3
+        # prefill with the residual stream split by token (all-to-all of head outputs)
+        # against the head all-gather with the whole O projection on every rank
+        pf = {}
+        for pmode in ("tokens", "gather"):
+            st = AttentionStack(num_layers=3, batch=4, max_seq_len=256, rank=rank, world=world,
+                                device=dev, seed=7, prefill_exchange=pmode)
+            pf[pmode] = st.prefill(prompt).cpu()
+            st.close()
+        checks["prefill_tokens_close_to_gather"] = _rel(pf["tokens"], pf["gather"]) < 1e-3
         torch.save({"checks": checks, "out": results["reduce"]}, Path(out_dir) / f"r{rank}.pt")
     finally:
         dist.destroy_process_group()
@@ -231,6 +240,7 @@ def test_peer_reduce_all_gpus(tmp_path):
         assert r["checks"] == {"eager_rel": True, "same_on_every_rank": True, "graph": True,
                                "no_timeout": True, "reduce_used_reduce": True,
                                "stack_errors_reduce": 0, "reduce_used_nccl": False,
-                               "stack_errors_nccl": 0, "stack_close_to_nccl": True}, r["checks"]
+                               "stack_errors_nccl": 0, "stack_close_to_nccl": True,
+                               "prefill_tokens_close_to_gather": True}, r["checks"]
     for r in res[1:]:
         assert torch.equal(res[0]["out"], r["out"])

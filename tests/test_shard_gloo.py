@@ -116,3 +116,50 @@ def test_peer_gather_rejects_one_buffer_over_two_ranks():
         assert p.exitcode == 0
     for r in range(2):
         assert "nbuf >= 2" in got[r], got[r]
+
+
+def _token_split_worker(rank, world, port, full, result_q):
+    import torch.distributed as dist
+    from fast_infer_b200.shard import gather_rows, heads_to_tokens, token_block
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        x = torch.from_numpy(full)                        # [T, heads * D], every rank
+        cols = x.shape[1] // world
+        mine = x[:, rank * cols:(rank + 1) * cols]        # this rank's heads, every token
+        t0, t1 = token_block(rank, world, x.shape[0])
+        rows = heads_to_tokens(mine)                      # every head, this rank's tokens
+        back = gather_rows(rows)                          # every head, every token
+        result_q.put((rank, torch.equal(rows, x[t0:t1]), torch.equal(back, x)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_heads_to_tokens_and_row_gather(world):
+    """The token-split prefill's two collectives: the all-to-all hands each rank every
+    head of its own token block (head order kept), and the row all-gather puts the
+    blocks back in token order, bit for bit."""
+    rng = np.random.default_rng(world)
+    full = rng.standard_normal((6 * world, 4 * world * 8), dtype=np.float32).astype(np.float16)
+    ctx = mp.get_context("spawn")
+    result_q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_token_split_worker, args=(r, world, port, full, result_q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = [result_q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, rows_ok, back_ok in got:
+        assert rows_ok and back_ok, (rank, rows_ok, back_ok)
+
+
+def test_token_block_rejects_uneven_split():
+    from fast_infer_b200.shard import token_block
+    assert token_block(2, 4, 16) == (8, 12)
+    with pytest.raises(ValueError):
+        token_block(0, 3, 16)
