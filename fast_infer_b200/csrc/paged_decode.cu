@@ -36,6 +36,12 @@ namespace fi {
 
 constexpr int kD = 128;
 constexpr int kPage = 64;
+// K/V pages are read once per call: their TMA copies carry an L2 evict-first policy,
+// so the stream does not push the block table, the queries and the partials (or a
+// neighbouring kernel's data) out of L2.
+#ifndef FI_DEC_EVICT_FIRST
+#define FI_DEC_EVICT_FIRST 1
+#endif
 constexpr int kDecWarps = 4;  // consumer warps of a page group (16 rows each)
 // Threads of a CTA whose kGrp groups of 4 consumer warps take alternate pages.
 __host__ __device__ constexpr int dec_threads(int kgrp) { return (kDecWarps * kgrp + 1) * 32; }
@@ -270,10 +276,18 @@ __global__ void __launch_bounds__(dec_threads(kGrp), kGrp == 1 ? (kSt == 2 ? 3 :
         }
         uint8_t* st = smem + s * kStageBytes;
         mbar_arrive_expect_tx(&full[s], kStageBytes);
+#if FI_DEC_EVICT_FIRST
+        const uint64_t pol = l2_policy_evict_first();
+        tma_load_4d_hint(st, &tm_k, &full[s], 0, kvh, 0, ph, pol);
+        tma_load_4d_hint(st + kRegionBytes, &tm_k, &full[s], 64, kvh, 0, ph, pol);
+        tma_load_4d_hint(st + 2 * kRegionBytes, &tm_v, &full[s], 0, kvh, 0, ph, pol);
+        tma_load_4d_hint(st + 3 * kRegionBytes, &tm_v, &full[s], 64, kvh, 0, ph, pol);
+#else
         tma_load_4d(st, &tm_k, &full[s], 0, kvh, 0, ph);
         tma_load_4d(st + kRegionBytes, &tm_k, &full[s], 64, kvh, 0, ph);
         tma_load_4d(st + 2 * kRegionBytes, &tm_v, &full[s], 0, kvh, 0, ph);
         tma_load_4d(st + 3 * kRegionBytes, &tm_v, &full[s], 64, kvh, 0, ph);
+#endif
       }
     }
     __syncthreads();  // pairs with the consumers' barrier before the merge

@@ -29,6 +29,19 @@
 
 namespace fi {
 
+#ifndef FI_SG_EVICT_FIRST
+#define FI_SG_EVICT_FIRST 1
+#endif
+// A weight tile: every weight byte is read once per call, so it may leave L2 first.
+__device__ __forceinline__ void sg_load_w(void* dst, const CUtensorMap* m, uint64_t* bar, int c0,
+                                          int c1, int c2) {
+#if FI_SG_EVICT_FIRST
+  tma_load_3d_hint(dst, m, bar, c0, c1, c2, l2_policy_evict_first());
+#else
+  tma_load_3d(dst, m, bar, c0, c1, c2);
+#endif
+}
+
 constexpr int kSgWarps = 8;                        // math warps
 constexpr int kSgThreads = (kSgWarps + 1) * 32;    // + one TMA producer warp
 constexpr int kSgRows = 16;                        // weight rows (outputs) per work item
@@ -100,8 +113,8 @@ __global__ void __launch_bounds__(kSgThreads, 1)
         const int item = blockIdx.x + (q / a.rounds) * gridDim.x, r = q % a.rounds;
         if (q < pre) {
           mbar_arrive_expect_tx(&bars->full[q], kSgStageBytes);
-          tma_load_3d(stages + q * kSgStageBytes, &tm_w, &bars->full[q], 0, item * kSgRows,
-                      r * kSgWarps);
+          sg_load_w(stages + q * kSgStageBytes, &tm_w, &bars->full[q], 0, item * kSgRows,
+                    r * kSgWarps);
         } else {
           tma_prefetch_l2_3d(&tm_w, 0, item * kSgRows, r * kSgWarps);
         }
@@ -115,8 +128,8 @@ __global__ void __launch_bounds__(kSgThreads, 1)
         const int item = blockIdx.x + (q / a.rounds) * gridDim.x, r = q % a.rounds;
         mbar_arrive_expect_tx(&bars->full[st], kSgStageBytes);
         // (element, row, 64-element chunk): 8 chunks x 16 rows x 128 bytes
-        tma_load_3d(stages + st * kSgStageBytes, &tm_w, &bars->full[st], 0, item * kSgRows,
-                    r * kSgWarps);
+        sg_load_w(stages + st * kSgStageBytes, &tm_w, &bars->full[st], 0, item * kSgRows,
+                  r * kSgWarps);
       }
       for (int q = total > kSgStages ? total - kSgStages : 0; q < total; ++q)
         mbar_wait(&bars->full[q % kSgStages], (q / kSgStages) & 1, a.err);
@@ -375,8 +388,8 @@ __global__ void __launch_bounds__(kSgThreads, kSsStages == 2 ? 3 : 2)
       const int pre = a.w_static ? (total < kSsStages ? total : kSsStages) : 0;
       for (int q = 0; q < pre; ++q) {
         mbar_arrive_expect_tx(&bars->full[q], kSsStageBytes);
-        tma_load_3d(stages + q * kSsStageBytes, &tm_w, &bars->full[q], 0,
-                    (blockIdx.x + (q / a.rounds) * gridDim.x) * kSgRows, (q % a.rounds) * kSgWarps);
+        sg_load_w(stages + q * kSsStageBytes, &tm_w, &bars->full[q], 0,
+                  (blockIdx.x + (q / a.rounds) * gridDim.x) * kSgRows, (q % a.rounds) * kSgWarps);
       }
       for (int q = pre; q < total && q < kSsStages; ++q)  // weights only to L2 before the wait
         tma_prefetch_l2_3d(&tm_w, 0, (blockIdx.x + (q / a.rounds) * gridDim.x) * kSgRows,
@@ -391,7 +404,7 @@ __global__ void __launch_bounds__(kSgThreads, kSsStages == 2 ? 3 : 2)
         uint8_t* sp = stages + st * kSsStageBytes;
         if (q >= pre) {
           mbar_arrive_expect_tx(&bars->full[st], kSsStageBytes);
-          tma_load_3d(sp, &tm_w, &bars->full[st], 0, item * kSgRows, r * kSgWarps);
+          sg_load_w(sp, &tm_w, &bars->full[st], 0, item * kSgRows, r * kSgWarps);
         }
         // x rows past M read as zeros (outside the tensor)
         tma_load_3d(sp + kSgStageBytes, &tm_x, &bars->full[st], 0, 0, r * kSgWarps);
