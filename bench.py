@@ -43,8 +43,9 @@ C3_SEQS, C3_LO, C3_HI, C3_SEED = 64, 512, 4096, 2
 PF_B, PF_S, PF_SEED = 4, 2048, 1
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) per paged_decode_kernel launch on this workload's shape,
-# from one `ncu --set full` capture of this workload shape: 2.7375 GB read + 8.9 MB written.
-DECODE_TRAFFIC_NCU = 2.7375e9 + 8.925e6
+# from one ncu capture of this workload shape (evict-first K/V loads): 2.7374 GB read +
+# 6.1 MB written.
+DECODE_TRAFFIC_NCU = 2.737407e9 + 6.11712e6
 # INT4 projections of one Llama-3.2-3B layer: (name, N = out features, K = in features).
 INT4_SHAPES = (("qkv", 5120, 3072), ("o", 3072, 3072), ("gate_up", 16384, 3072),
                ("down", 3072, 8192))
