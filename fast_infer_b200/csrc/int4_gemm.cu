@@ -14,9 +14,10 @@
 // fi_int4_gemm (M <= 64) streams the 4-bit weights once from HBM:
 // * Persistent CTAs of one or two groups of (one producer warp + 8 consumer warps)
 //   sharing x staged in shared memory. Each group's producer streams
-//   16-row x 512-byte weight tiles (1024 k) with TMA into a shared-memory ring (one
-//   3-D box of 4 x 128-byte chunks per tile, 128B-swizzled so the consumers' 16-byte
-//   reads are conflict-free); each consumer warp takes 128 k of every tile.
+//   R-row x 512-byte weight tiles (1024 k; R = 16, or 8 where that balances the SMs)
+//   with TMA into a shared-memory ring (one 3-D box of 4 x 128-byte chunks per tile,
+//   128B-swizzled so the consumers' 16-byte reads are conflict-free); each consumer
+//   warp takes 128 k of every tile.
 // * Nibbles become fp16 without a conversion instruction: lop3 drops a nibble (sign
 //   bit flipped) into the mantissa of 1024.0 (0x6400) in each half of a register, an
 //   exact f16x2 subtract / fma removes the offset, and an f16x2 multiply by the group
@@ -36,17 +37,15 @@ namespace fi {
 
 constexpr int kI4Consumers = 8;                         // math warps of a group
 constexpr int kI4Threads = (kI4Consumers + 1) * 32;     // + one TMA producer warp
-constexpr int kI4Rows = 16;        // weight rows (output columns) per work item
+constexpr int kI4Rows = 16;        // weight rows (output columns) per work item, at most
 constexpr int kI4KIter = 128;      // k per consumer warp per round: 4 threads x 32 nibbles
 constexpr int kI4RoundK = kI4Consumers * kI4KIter;      // 1024 k per round
-constexpr int kI4BoxBytes = 128;   // one 128B-swizzled TMA box: 16 rows x 128 packed bytes
+constexpr int kI4BoxBytes = 128;   // one 128B-swizzled TMA box: R rows x 128 packed bytes
 constexpr int kI4Boxes = kI4RoundK / 2 / kI4BoxBytes;   // 4 boxes per stage
-constexpr int kI4StageBytes = kI4Rows * kI4RoundK / 2;  // 8 KB
 #ifndef FI_I4_STAGES
 #define FI_I4_STAGES 6
 #endif
 constexpr int kI4Stages = FI_I4_STAGES;
-constexpr int kI4ScaleBytes = kI4Rows * (kI4RoundK / 128) * 2;  // 256: 16 rows x 8 fp16
 constexpr int kI4XBatch = 8;      // x chunks each thread loads at once when staging
 constexpr int kI4MaxM = 64;        // up to eight 8-token tiles
 constexpr int kI4ConsumerBar = 1;  // named barrier of the 256 consumer threads
@@ -63,23 +62,37 @@ struct I4Args {
   int64_t xs0, ss0, ss1, cs0, cs1;
 };
 
-// Item epilogue buffer in shared memory: consumer warps x 8*NT tokens x 17 floats
-// (16 rows + 1 of padding).
-template <int NT>
+// A work item is R = 16 weight rows (the whole M of the m16n8k16 A operand) or R = 8
+// (rows 8-15 of the A operand zero; batches of up to 8 tokens): where 16-row items leave
+// some SMs one item more than others, 8-row items halve that overhang. An R-row stage is R x 512 bytes, and
+// the 8-row ring has twice the stages, so the bytes in flight stay the same.
+template <int R>
+__host__ __device__ constexpr int i4_stage_bytes() { return R * kI4RoundK / 2; }
+template <int R>
+__host__ __device__ constexpr int i4_scale_bytes() { return R * (kI4RoundK / 128) * 2; }
+template <int R>
+__host__ __device__ constexpr int i4_stages() {
+  return R == kI4Rows ? kI4Stages : 2 * kI4Stages;
+}
+
+// Item epilogue buffer in shared memory: consumer warps x 8*NT tokens x (R + 1) floats
+// (R rows + 1 of padding).
+template <int NT, int R>
 __host__ __device__ constexpr size_t i4_red_bytes() {
-  return (size_t)kI4Consumers * NT * 8 * (kI4Rows + 1) * 4;
+  return (size_t)kI4Consumers * NT * 8 * (R + 1) * 4;
 }
 
 // One group's shared memory: weight ring, scale ring, barriers, epilogue buffer,
 // rounded up to 1024 bytes so every group's ring keeps the swizzle alignment.
-template <int NT>
+template <int NT, int R>
 __host__ __device__ constexpr size_t i4_group_bytes() {
-  return ((size_t)kI4Stages * (kI4StageBytes + kI4ScaleBytes) + 256 + i4_red_bytes<NT>() + 1023) /
+  return ((size_t)i4_stages<R>() * (i4_stage_bytes<R>() + i4_scale_bytes<R>()) + 256 +
+          i4_red_bytes<NT, R>() + 1023) /
          1024 * 1024;
 }
 
-struct I4Bars {
-  uint64_t full[kI4Stages], empty[kI4Stages];
+struct I4Bars {  // sized for the deeper (8-row) ring: 192 of the 256 bytes reserved
+  uint64_t full[2 * kI4Stages], empty[2 * kI4Stages];
 };
 
 // (a & b) ^ c
@@ -168,12 +181,12 @@ __device__ __forceinline__ void i4_load_3d(void* dst, const CUtensorMap* m, uint
 #endif
 }
 
-// Persistent: CTA b takes work items b, b + grid, ... ; an item = 16 weight rows x all
+// Persistent: CTA b takes work items b, b + grid, ... ; an item = R weight rows x all
 // of K, processed in rounds of 1024 k. The producer warp streams each round's
-// 16 x 512-byte weight tile into a kI4Stages ring as [4 chunks][16 rows][128 bytes],
-// 128B-swizzled;
+// R x 512-byte weight tile into a ring as [4 chunks][R rows][128 bytes], 128B-swizzled;
 // consumer warp w multiplies k = round*1024 + w*128 + 32t .. +32 of both 8-row halves
-// (rows g and g+8 of the tile) against x, computing C^T = W x^T with the weight rows
+// (rows g and g+8 of the tile; g+8 only when R = 16) against x, computing C^T = W x^T
+// with the weight rows
 // as the MMA's M dimension and the tokens as N (tiles of 8). At the end of an item the
 // 8 warps add their partial sums in warp order through shared memory.
 // kSmemX: x is staged once into shared memory (rows < M, each 8-group in the order
@@ -189,7 +202,7 @@ __device__ __forceinline__ void i4_load_3d(void* dst, const CUtensorMap* m, uint
 // Launched with programmatic dependent launch: the producer pulls its first ring of
 // weight tiles into L2 while the previous kernel finishes; every read of x, of the
 // scales and of the ring waits for it (grid_dep_wait).
-template <int NT, bool kSmemX, int G>
+template <int NT, bool kSmemX, int G, int R>
 __global__ void __launch_bounds__(G * kI4Threads, NT == 1 ? 32 / kI4Consumers : 1)
     int4_gemm_kernel(const __grid_constant__ CUtensorMap tm_w,
                      const __grid_constant__ CUtensorMap tm_s, const I4Args a) {
@@ -201,22 +214,24 @@ __global__ void __launch_bounds__(G * kI4Threads, NT == 1 ? 32 / kI4Consumers : 
   const int grp = warp_all / (kI4Consumers + 1);
   const int warp = warp_all - grp * (kI4Consumers + 1);  // warp within the group
   const int tid = warp * 32 + lane;                       // thread within the group
-  uint8_t* stages = smem + grp * i4_group_bytes<NT>();
-  uint8_t* sstages = stages + kI4Stages * kI4StageBytes;  // kI4Stages x 256-byte scale tiles
-  I4Bars* bars = reinterpret_cast<I4Bars*>(sstages + kI4Stages * kI4ScaleBytes);
-  // partial sums of the item epilogue: [warp][token][row], rows padded to 17
-  auto red = reinterpret_cast<float(*)[NT * 8][kI4Rows + 1]>(reinterpret_cast<uint8_t*>(bars) + 256);
-  __half* xs = reinterpret_cast<__half*>(smem + G * i4_group_bytes<NT>());
+  constexpr int kSB = i4_stage_bytes<R>(), kScB = i4_scale_bytes<R>(), kSt = i4_stages<R>();
+  uint8_t* stages = smem + grp * i4_group_bytes<NT, R>();
+  uint8_t* sstages = stages + kSt * kSB;  // kSt scale tiles of R rows x 8 groups
+  I4Bars* bars = reinterpret_cast<I4Bars*>(sstages + kSt * kScB);
+  // partial sums of the item epilogue: [warp][token][row], rows padded to R + 1
+  auto red = reinterpret_cast<float(*)[NT * 8][R + 1]>(reinterpret_cast<uint8_t*>(bars) + 256);
+  __half* xs = reinterpret_cast<__half*>(smem + G * i4_group_bytes<NT, R>());
   const int group_bar = kI4ConsumerBar + grp;  // named barrier of this group's consumers
 
-  // Item slots: slot grp of CTA b is b*G + grp; it takes items slot, slot + grid*G, ...
-  const int items = (a.N + kI4Rows - 1) / kI4Rows;
-  const int slot = blockIdx.x * G + grp, nslots = gridDim.x * G;
+  // Item slots, group-major (slot grp * grid + b for group grp of CTA b), so items past
+  // one per slot go to different CTAs; a slot takes items slot, slot + grid*G, ...
+  const int items = (a.N + R - 1) / R;
+  const int slot = grp * gridDim.x + blockIdx.x, nslots = gridDim.x * G;
   const int my_items = slot < items ? (items - slot + nslots - 1) / nslots : 0;
   const int total = my_items * a.rounds;
 
   if (tid == 0) {
-    for (int i = 0; i < kI4Stages; ++i) {
+    for (int i = 0; i < kSt; ++i) {
       mbar_init(&bars->full[i], 1);
       mbar_init(&bars->empty[i], kI4Consumers * 32);
     }
@@ -235,42 +250,39 @@ __global__ void __launch_bounds__(G * kI4Threads, NT == 1 ? 32 / kI4Consumers : 
       // Before the previous kernel on the stream is known to be done (it may have
       // written these weights), the first ring's worth of weight tiles only goes to
       // L2; the shared-memory copies start after grid_dep_wait().
-      for (int q = 0; q < total && q < kI4Stages; ++q) {
+      for (int q = 0; q < total && q < kSt; ++q) {
         const int item = slot + (q / a.rounds) * nslots, r = q % a.rounds;
         if (a.tma3d) {
-          tma_prefetch_l2_3d(&tm_w, 0, item * kI4Rows, r * kI4Boxes);
+          tma_prefetch_l2_3d(&tm_w, 0, item * R, r * kI4Boxes);
         } else {
 #pragma unroll
           for (int b = 0; b < kI4Boxes; ++b)
-            tma_prefetch_l2_2d(&tm_w, r * (kI4RoundK / 2) + b * kI4BoxBytes, item * kI4Rows);
+            tma_prefetch_l2_2d(&tm_w, r * (kI4RoundK / 2) + b * kI4BoxBytes, item * R);
         }
       }
       grid_dep_wait();
       bool dead = false;
       for (int q = 0; q < total; ++q) {
-        const int st = q % kI4Stages;
-        if (q >= kI4Stages && !dead)
-          dead = !mbar_wait(&bars->empty[st], ((q / kI4Stages) - 1) & 1, a.err);
+        const int st = q % kSt;
+        if (q >= kSt && !dead) dead = !mbar_wait(&bars->empty[st], ((q / kSt) - 1) & 1, a.err);
         const int item = slot + (q / a.rounds) * nslots, r = q % a.rounds;
-        mbar_arrive_expect_tx(&bars->full[st],
-                              kI4StageBytes + (a.tma_scales ? kI4ScaleBytes : 0));
-        if (a.tma_scales)  // scales [N, K/128] fp16: 8 groups x 16 rows
-          i4_load_2d(sstages + st * kI4ScaleBytes, &tm_s, &bars->full[st],
-                     r * (kI4RoundK / 128), item * kI4Rows);
+        mbar_arrive_expect_tx(&bars->full[st], kSB + (a.tma_scales ? kScB : 0));
+        if (a.tma_scales)  // scales [N, K/128] fp16: 8 groups x R rows
+          i4_load_2d(sstages + st * kScB, &tm_s, &bars->full[st], r * (kI4RoundK / 128),
+                     item * R);
         if (a.tma3d) {
-          // (byte, row, 128-byte chunk): one box = 4 chunks x 16 rows x 128 bytes
-          i4_load_3d(stages + st * kI4StageBytes, &tm_w, &bars->full[st], 0, item * kI4Rows,
-                     r * kI4Boxes);
+          // (byte, row, 128-byte chunk): one box = 4 chunks x R rows x 128 bytes
+          i4_load_3d(stages + st * kSB, &tm_w, &bars->full[st], 0, item * R, r * kI4Boxes);
         } else {
 #pragma unroll
           for (int b = 0; b < kI4Boxes; ++b)
-            i4_load_2d(stages + st * kI4StageBytes + b * (kI4Rows * kI4BoxBytes), &tm_w,
-                       &bars->full[st], r * (kI4RoundK / 2) + b * kI4BoxBytes, item * kI4Rows);
+            i4_load_2d(stages + st * kSB + b * (R * kI4BoxBytes), &tm_w, &bars->full[st],
+                       r * (kI4RoundK / 2) + b * kI4BoxBytes, item * R);
         }
       }
       // Let the last copy of every stage land before the CTA can exit.
-      for (int q = total > kI4Stages ? total - kI4Stages : 0; q < total; ++q)
-        mbar_wait(&bars->full[q % kI4Stages], (q / kI4Stages) & 1, a.err);
+      for (int q = total > kSt ? total - kSt : 0; q < total; ++q)
+        mbar_wait(&bars->full[q % kSt], (q / kSt) & 1, a.err);
     }
     return;
   }
@@ -321,7 +333,7 @@ __global__ void __launch_bounds__(G * kI4Threads, NT == 1 ? 32 / kI4Consumers : 
 
   // scale of (row, k) for this lane; fetched one round ahead
   auto scale_of = [&](int item, int r, int h) -> uint16_t {
-    const int n = item * kI4Rows + g + 8 * h;
+    const int n = item * R + g + 8 * h;
     const int kk = r * kI4RoundK + warp * kI4KIter + 32 * t;
     if (n >= a.N || kk >= a.K) return 0;
     const int grp = a.gs_shift >= 0 ? kk >> a.gs_shift : kk / a.gs;
@@ -330,7 +342,7 @@ __global__ void __launch_bounds__(G * kI4Threads, NT == 1 ? 32 / kI4Consumers : 
   uint16_t sa_n = 0, sb_n = 0;
   if (total > 0 && !a.tma_scales) {
     sa_n = scale_of(slot, 0, 0);
-    sb_n = scale_of(slot, 0, 1);
+    if constexpr (R == kI4Rows) sb_n = scale_of(slot, 0, 1);
   }
 
   float acc[NT][4];
@@ -343,6 +355,7 @@ __global__ void __launch_bounds__(G * kI4Threads, NT == 1 ? 32 / kI4Consumers : 
   const int box = warp >> 1;                 // which 128-byte box of the stage
   const int chunk = ((warp & 1) << 2) + t;   // 16-byte chunk inside the box row
   const int swz = (chunk ^ g) << 4;          // 128B swizzle: chunk ^ (row % 8), row = g or g+8
+  // 8-row items: rows 8-15 of the A operand are zero (their outputs are not stored)
   int q = 0;
   for (int j = 0; j < my_items; ++j) {
     const int item = slot + j * nslots;
@@ -353,17 +366,19 @@ __global__ void __launch_bounds__(G * kI4Threads, NT == 1 ? 32 / kI4Consumers : 
         const int it1 = r + 1 < a.rounds ? item : item + nslots;
         const bool more = q + 1 < total;
         sa_n = more ? scale_of(it1, r1, 0) : 0;
-        sb_n = more ? scale_of(it1, r1, 1) : 0;
+        if constexpr (R == kI4Rows) sb_n = more ? scale_of(it1, r1, 1) : 0;
       }
-      const int st = q % kI4Stages;
-      if (!dead) dead = !__all_sync(0xffffffffu, mbar_wait(&bars->full[st], (q / kI4Stages) & 1, a.err));
-      const uint8_t* sbase = stages + st * kI4StageBytes + box * (kI4Rows * kI4BoxBytes);
+      const int st = q % kSt;
+      if (!dead) dead = !__all_sync(0xffffffffu, mbar_wait(&bars->full[st], (q / kSt) & 1, a.err));
+      const uint8_t* sbase = stages + st * kSB + box * (R * kI4BoxBytes);
       const uint4 qa4 = *reinterpret_cast<const uint4*>(sbase + g * kI4BoxBytes + swz);
-      const uint4 qb4 = *reinterpret_cast<const uint4*>(sbase + (g + 8) * kI4BoxBytes + swz);
-      if (a.tma_scales) {  // [16 rows][groups of the round]: this warp's group is `warp`
-        const uint16_t* sc = reinterpret_cast<const uint16_t*>(sstages + st * kI4ScaleBytes);
+      uint4 qb4 = make_uint4(0u, 0u, 0u, 0u);
+      if constexpr (R == kI4Rows)
+        qb4 = *reinterpret_cast<const uint4*>(sbase + (g + 8) * kI4BoxBytes + swz);
+      if (a.tma_scales) {  // [R rows][groups of the round]: this warp's group is `warp`
+        const uint16_t* sc = reinterpret_cast<const uint16_t*>(sstages + st * kScB);
         s2a = splat16(sc[g * (kI4RoundK / 128) + warp]);
-        s2b = splat16(sc[(g + 8) * (kI4RoundK / 128) + warp]);
+        if constexpr (R == kI4Rows) s2b = splat16(sc[(g + 8) * (kI4RoundK / 128) + warp]);
       }
       // The stage is released before these values are used, and the next write to it
       // is a TMA (async proxy) write: order this thread's generic reads before it.
@@ -375,13 +390,13 @@ __global__ void __launch_bounds__(G * kI4Threads, NT == 1 ? 32 / kI4Consumers : 
       const uint32_t wb4[4] = {qb4.x, qb4.y, qb4.z, qb4.w};
 #pragma unroll
       for (int wd = 0; wd < 4; ++wd) {
-        uint32_t ba[4], bb[4];
+        uint32_t ba[4], bb[4] = {0u, 0u, 0u, 0u};
         if constexpr (kSmemX) {
           dequant_word_perm(wa4[wd], s2a, ba);
-          dequant_word_perm(wb4[wd], s2b, bb);
+          if constexpr (R == kI4Rows) dequant_word_perm(wb4[wd], s2b, bb);
         } else {
           dequant_word(wa4[wd], s2a, ba);
-          dequant_word(wb4[wd], s2b, bb);
+          if constexpr (R == kI4Rows) dequant_word(wb4[wd], s2b, bb);
         }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
@@ -405,13 +420,14 @@ __global__ void __launch_bounds__(G * kI4Threads, NT == 1 ? 32 / kI4Consumers : 
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         // C^T fragment: weight row g + 8*(e>>1), token nt*8 + 2t + (e&1)
-        red[warp][nt * 8 + 2 * t + (e & 1)][g + (e >> 1) * 8] = acc[nt][e];
+        if (R == kI4Rows || e < 2)
+          red[warp][nt * 8 + 2 * t + (e & 1)][g + (e >> 1) * 8] = acc[nt][e];
         acc[nt][e] = 0.f;
       }
     named_bar_sync(group_bar, kI4Consumers * 32);
-    const int nbase = item * kI4Rows;
-    for (int i = tid; i < a.M * kI4Rows; i += kI4Consumers * 32) {
-      const int m = i / kI4Rows, rr = i - m * kI4Rows, n = nbase + rr;
+    const int nbase = item * R;
+    for (int i = tid; i < a.M * R; i += kI4Consumers * 32) {
+      const int m = i / R, rr = i - m * R, n = nbase + rr;
       float sum = 0.f;
 #pragma unroll
       for (int w = 0; w < kI4Consumers; ++w) sum += red[w][m][rr];
@@ -442,47 +458,48 @@ __global__ void __launch_bounds__(256) int4_dequant_kernel(const uint8_t* w, con
 constexpr size_t kI4SmemOptin = 232448;  // per-block shared memory limit (227 KB)
 
 // Dynamic shared memory without x: 1 KB of alignment slack and G groups.
-template <int NT, int G>
+template <int NT, int G, int R>
 constexpr size_t i4_smem_base() {
-  return 1024 + (size_t)G * i4_group_bytes<NT>();
+  return 1024 + (size_t)G * i4_group_bytes<NT, R>();
 }
 
 // Largest staged x for an instance: the limit minus the groups, less 1 KB of margin.
 #ifndef FI_I4_XMAX_KB
 #define FI_I4_XMAX_KB 1024
 #endif
-template <int NT, int G>
+template <int NT, int G, int R>
 constexpr size_t i4_smem_x_max() {
-  constexpr size_t used = i4_smem_base<NT, G>() + 1024;
+  constexpr size_t used = i4_smem_base<NT, G, R>() + 1024;
   constexpr size_t fit = used < kI4SmemOptin ? kI4SmemOptin - used : 0;
   return fit < (size_t)FI_I4_XMAX_KB * 1024 ? fit : (size_t)FI_I4_XMAX_KB * 1024;
 }
 
 // Opts each instance in to its largest shared-memory layout (once per device), sizes
 // the persistent grid with the occupancy calculator for this call's layout, launches.
-template <int NT, bool kSmemX, int G>
+template <int NT, bool kSmemX, int G, int R>
 static int launch_int4_gemm(cudaStream_t st, const CUtensorMap& tm, const CUtensorMap& tms,
                             const I4Args& a) {
   static DeviceOnce attr_once;
   {
     const cudaError_t e = attr_once.run([] {
-      const int max_smem = (int)(i4_smem_base<NT, G>() + (kSmemX ? i4_smem_x_max<NT, G>() : 0));
-      return cudaFuncSetAttribute(int4_gemm_kernel<NT, kSmemX, G>,
+      const int max_smem =
+          (int)(i4_smem_base<NT, G, R>() + (kSmemX ? i4_smem_x_max<NT, G, R>() : 0));
+      return cudaFuncSetAttribute(int4_gemm_kernel<NT, kSmemX, G, R>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
     });
     if (e != cudaSuccess) return cuda_fail(e, "fi_int4_gemm: cudaFuncSetAttribute");
   }
   const size_t smem =
-      i4_smem_base<NT, G>() + (kSmemX ? (size_t)a.M * (size_t)a.xstride * 2 : 0);
+      i4_smem_base<NT, G, R>() + (kSmemX ? (size_t)a.M * (size_t)a.xstride * 2 : 0);
   const int threads = G * kI4Threads;
   int nb = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, int4_gemm_kernel<NT, kSmemX, G>,
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, int4_gemm_kernel<NT, kSmemX, G, R>,
                                                     threads, smem) != cudaSuccess || nb < 1)
     nb = 1;
-  const int items = (a.N + kI4Rows - 1) / kI4Rows;
+  const int items = (a.N + R - 1) / R;
   int grid = nb * sm_count();
   if (grid > (items + G - 1) / G) grid = (items + G - 1) / G;
-  cudaError_t e = launch_pdl(int4_gemm_kernel<NT, kSmemX, G>, dim3((unsigned)grid),
+  cudaError_t e = launch_pdl(int4_gemm_kernel<NT, kSmemX, G, R>, dim3((unsigned)grid),
                              dim3(threads), smem, st, tm, tms, a);
   if (e != cudaSuccess) return cuda_fail(e, "fi_int4_gemm launch");
   return FI_OK;
@@ -490,16 +507,35 @@ static int launch_int4_gemm(cudaStream_t st, const CUtensorMap& tm, const CUtens
 
 // x staged in shared memory when it fits; for two 8-token tiles (9-16 tokens) two
 // groups share one staged x when both rings fit beside it (16 math warps per SM).
-template <int NT>
+template <int NT, int R>
 static int launch_int4_gemm_nt(cudaStream_t st, const CUtensorMap& tm, const CUtensorMap& tms,
                                const I4Args& a) {
   const size_t xbytes = (size_t)a.M * (size_t)a.xstride * 2;
   if constexpr (NT == 2) {
-    if (xbytes <= i4_smem_x_max<NT, 2>())
-      return launch_int4_gemm<NT, true, 2>(st, tm, tms, a);
+    if (xbytes <= i4_smem_x_max<NT, 2, R>())
+      return launch_int4_gemm<NT, true, 2, R>(st, tm, tms, a);
   }
-  if (xbytes <= i4_smem_x_max<NT, 1>()) return launch_int4_gemm<NT, true, 1>(st, tm, tms, a);
-  return launch_int4_gemm<NT, false, 1>(st, tm, tms, a);
+  if (xbytes <= i4_smem_x_max<NT, 1, R>()) return launch_int4_gemm<NT, true, 1, R>(st, tm, tms, a);
+  return launch_int4_gemm<NT, false, 1, R>(st, tm, tms, a);
+}
+
+// Rows per work item for batches of up to 8 tokens: 8 when 16-row items number at most
+// two per SM and 8-row items lower the most rows any SM streams, else 16. N = 3072 on
+// 148 SMs: 192 items of 16 leave 44 SMs two (32 rows), 384 items of 8 give every SM at
+// most three (24 rows). Measured per call (CUDA graphs, weights rotated past L2, batch
+// 1, K = 3072 / 8192, 16-row / 8-row): N = 3072 4.73 / 4.18 and 9.17 / 8.61 us, N = 1184
+// 3.04 / 2.79 and 5.96 / 5.17; above two items per SM 8-row items lose (N = 5120: 5.11
+// / 6.58, 11.36 / 14.2), as they do at 9-16 tokens (N = 3072, K = 8192: 16.7 / 23.5).
+#ifndef FI_I4_ROWS8
+#define FI_I4_ROWS8 1
+#endif
+static int int4_rows_per_item(int64_t m, int64_t n) {
+  if (!FI_I4_ROWS8 || m > 8) return kI4Rows;
+  const int64_t sms = sm_count();
+  const int64_t load16 = (n + 15) / 16, load8 = (n + 7) / 8;
+  if (load16 > 2 * sms) return kI4Rows;
+  const int64_t max16 = (load16 + sms - 1) / sms * 16, max8 = (load8 + sms - 1) / sms * 8;
+  return max8 < max16 ? 8 : kI4Rows;
 }
 
 }  // namespace fi
@@ -536,23 +572,24 @@ extern "C" int fi_int4_gemm(const void* x, const void* packed, const void* scale
                 "fi_int4_gemm packed: needs a 16-byte aligned base, unit stride along K/2 and a "
                 "row stride that is a multiple of 16 bytes");
   // packed [N, K/2] bytes through a tensor map with 128B swizzle. When K/2 is a whole
-  // number of 128-byte chunks: 3-D (byte, row, chunk), one 4-chunk x 16-row box per
-  // stage; otherwise 2-D (byte, row) with four 128 x 16 boxes (the 3-D view would let
+  // number of 128-byte chunks: 3-D (byte, row, chunk), one 4-chunk x R-row box per
+  // stage; otherwise 2-D (byte, row) with four 128 x R boxes (the 3-D view would let
   // the last chunk of the last row run past the tensor).
   CUtensorMap tm;
   const int tma3d = (k / 2) % kI4BoxBytes == 0 ? 1 : 0;
+  const int rows = int4_rows_per_item(m, n);  // weight rows per work item (TMA box height)
   int r;
   if (tma3d) {
     const uint64_t dims[3] = {(uint64_t)kI4BoxBytes, (uint64_t)n,
                               (uint64_t)(k / 2 / kI4BoxBytes)};
     const uint64_t sb[2] = {(uint64_t)packed_strides[0], (uint64_t)kI4BoxBytes};
-    const uint32_t box[3] = {(uint32_t)kI4BoxBytes, (uint32_t)kI4Rows, (uint32_t)kI4Boxes};
+    const uint32_t box[3] = {(uint32_t)kI4BoxBytes, (uint32_t)rows, (uint32_t)kI4Boxes};
     r = encode_tiled(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, packed, dims, sb, box,
                      CU_TENSOR_MAP_SWIZZLE_128B, "fi_int4_gemm packed");
   } else {
     const uint64_t dims[2] = {(uint64_t)(k / 2), (uint64_t)n};
     const uint64_t sb[1] = {(uint64_t)packed_strides[0]};
-    const uint32_t box[2] = {(uint32_t)kI4BoxBytes, (uint32_t)kI4Rows};
+    const uint32_t box[2] = {(uint32_t)kI4BoxBytes, (uint32_t)rows};
     r = encode_tiled(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, packed, dims, sb, box,
                      CU_TENSOR_MAP_SWIZZLE_128B, "fi_int4_gemm packed");
   }
@@ -579,7 +616,7 @@ extern "C" int fi_int4_gemm(const void* x, const void* packed, const void* scale
   if (a.tma_scales) {
     const uint64_t sdims[2] = {(uint64_t)(k / 128), (uint64_t)n};
     const uint64_t ssb[1] = {(uint64_t)scales_strides[0] * 2};
-    const uint32_t sbox[2] = {(uint32_t)(kI4RoundK / 128), (uint32_t)kI4Rows};
+    const uint32_t sbox[2] = {(uint32_t)(kI4RoundK / 128), (uint32_t)rows};
     r = encode_tiled(&tms, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, scales, sdims, ssb, sbox,
                      CU_TENSOR_MAP_SWIZZLE_NONE, "fi_int4_gemm scales");
     if (r != FI_OK) return r;
@@ -591,10 +628,12 @@ extern "C" int fi_int4_gemm(const void* x, const void* packed, const void* scale
   a.cs1 = c_strides[1];
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // 8-token tiles: 1, 2, 4 or 8
-  if (m <= 8) r = launch_int4_gemm_nt<1>(st, tm, tms, a);
-  else if (m <= 16) r = launch_int4_gemm_nt<2>(st, tm, tms, a);
-  else if (m <= 32) r = launch_int4_gemm_nt<4>(st, tm, tms, a);
-  else r = launch_int4_gemm_nt<8>(st, tm, tms, a);
+  if (m <= 8)
+    r = rows == 8 ? launch_int4_gemm_nt<1, 8>(st, tm, tms, a)
+                  : launch_int4_gemm_nt<1, kI4Rows>(st, tm, tms, a);
+  else if (m <= 16) r = launch_int4_gemm_nt<2, kI4Rows>(st, tm, tms, a);
+  else if (m <= 32) r = launch_int4_gemm_nt<4, kI4Rows>(st, tm, tms, a);
+  else r = launch_int4_gemm_nt<8, kI4Rows>(st, tm, tms, a);
   if (r != FI_OK) return r;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "fi_int4_gemm launch");
