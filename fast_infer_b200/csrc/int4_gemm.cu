@@ -49,6 +49,7 @@ constexpr int kI4Stages = FI_I4_STAGES;
 constexpr int kI4XBatch = 8;      // x chunks each thread loads at once when staging
 constexpr int kI4MaxM = 64;        // up to eight 8-token tiles
 constexpr int kI4ConsumerBar = 1;  // named barrier of the 256 consumer threads
+constexpr int kI4XRItems = 2;      // most items per slot when x is staged round by round
 
 struct I4Args {
   const __half* x;
@@ -63,9 +64,10 @@ struct I4Args {
 };
 
 // A work item is R = 16 weight rows (the whole M of the m16n8k16 A operand) or R = 8
-// (rows 8-15 of the A operand zero; batches of up to 8 tokens): where 16-row items leave
-// some SMs one item more than others, 8-row items halve that overhang. An R-row stage is R x 512 bytes, and
-// the 8-row ring has twice the stages, so the bytes in flight stay the same.
+// (rows 8-15 of the A operand zero; batches of up to 8 tokens): where 16-row items
+// leave some SMs one item more than others, 8-row items halve that overhang. An R-row
+// stage is R x 512 bytes, and the 8-row ring has twice the stages, so the bytes in
+// flight stay the same.
 template <int R>
 __host__ __device__ constexpr int i4_stage_bytes() { return R * kI4RoundK / 2; }
 template <int R>
@@ -202,7 +204,11 @@ __device__ __forceinline__ void i4_load_3d(void* dst, const CUtensorMap* m, uint
 // Launched with programmatic dependent launch: the producer pulls its first ring of
 // weight tiles into L2 while the previous kernel finishes; every read of x, of the
 // scales and of the ring waits for it (grid_dep_wait).
-template <int NT, bool kSmemX, int G, int R>
+// kXR (x too large for shared memory, 9-16 tokens): x is staged one 1024-k round at a
+// time into two shared-memory slices that the groups share, and each slot's items (at
+// most kI4XRItems) advance round by round, so x is read from L2 once per round instead
+// of once per weight word.
+template <int NT, bool kSmemX, int G, int R, bool kXR = false>
 __global__ void __launch_bounds__(G * kI4Threads, NT == 1 ? 32 / kI4Consumers : 1)
     int4_gemm_kernel(const __grid_constant__ CUtensorMap tm_w,
                      const __grid_constant__ CUtensorMap tm_s, const I4Args a) {
@@ -229,6 +235,11 @@ __global__ void __launch_bounds__(G * kI4Threads, NT == 1 ? 32 / kI4Consumers : 
   const int slot = grp * gridDim.x + blockIdx.x, nslots = gridDim.x * G;
   const int my_items = slot < items ? (items - slot + nslots - 1) / nslots : 0;
   const int total = my_items * a.rounds;
+  // Stage q of this slot: item-major, or round-major when x is staged by round.
+  auto q_item = [&](int q) {
+    return slot + (kXR ? q % my_items : q / a.rounds) * nslots;
+  };
+  auto q_round = [&](int q) { return kXR ? q / my_items : q % a.rounds; };
 
   if (tid == 0) {
     for (int i = 0; i < kSt; ++i) {
@@ -251,7 +262,7 @@ __global__ void __launch_bounds__(G * kI4Threads, NT == 1 ? 32 / kI4Consumers : 
       // written these weights), the first ring's worth of weight tiles only goes to
       // L2; the shared-memory copies start after grid_dep_wait().
       for (int q = 0; q < total && q < kSt; ++q) {
-        const int item = slot + (q / a.rounds) * nslots, r = q % a.rounds;
+        const int item = q_item(q), r = q_round(q);
         if (a.tma3d) {
           tma_prefetch_l2_3d(&tm_w, 0, item * R, r * kI4Boxes);
         } else {
@@ -265,7 +276,7 @@ __global__ void __launch_bounds__(G * kI4Threads, NT == 1 ? 32 / kI4Consumers : 
       for (int q = 0; q < total; ++q) {
         const int st = q % kSt;
         if (q >= kSt && !dead) dead = !mbar_wait(&bars->empty[st], ((q / kSt) - 1) & 1, a.err);
-        const int item = slot + (q / a.rounds) * nslots, r = q % a.rounds;
+        const int item = q_item(q), r = q_round(q);
         mbar_arrive_expect_tx(&bars->full[st], kSB + (a.tma_scales ? kScB : 0));
         if (a.tma_scales)  // scales [N, K/128] fp16: 8 groups x R rows
           i4_load_2d(sstages + st * kScB, &tm_s, &bars->full[st], r * (kI4RoundK / 128),
@@ -328,7 +339,112 @@ __global__ void __launch_bounds__(G * kI4Threads, NT == 1 ? 32 / kI4Consumers : 
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const int tok = min(nt * 8 + g, a.M - 1);
-    xo[nt] = kSmemX ? (int64_t)tok * a.xstride : (int64_t)tok * a.xs0;
+    xo[nt] = kXR ? (int64_t)tok * (kI4RoundK + 8)
+                 : kSmemX ? (int64_t)tok * a.xstride : (int64_t)tok * a.xs0;
+  }
+
+  if constexpr (kXR) {
+    // Requires scales by TMA (the host checks) and at most kI4XRItems items per slot.
+    constexpr int kXS = kI4RoundK + 8;   // slice row stride (halves)
+    constexpr int kC8 = kI4RoundK / 8;   // 16-byte chunks per slice row
+    constexpr int kAll = G * kI4Consumers * 32;
+    const int xtid = grp * kI4Consumers * 32 + tid;
+    // slice r of x into dst, pair order as for the whole staged x, 4 loads in flight
+    auto stage_x = [&](int r, __half* dst) {
+      const int n = a.M * kC8;
+      for (int c0 = xtid; c0 < n; c0 += 4 * kAll) {
+        uint4 u[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = c0 + j * kAll, m = c / kC8, k0 = r * kI4RoundK + (c - m * kC8) * 8;
+          u[j] = make_uint4(0u, 0u, 0u, 0u);
+          if (c < n && k0 < a.K)
+            u[j] = *reinterpret_cast<const uint4*>(a.x + (int64_t)m * a.xs0 + k0);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = c0 + j * kAll, m = c / kC8;
+          if (c < n)
+            *reinterpret_cast<uint4*>(dst + m * kXS + (c - m * kC8) * 8) = make_uint4(
+                __byte_perm(u[j].x, u[j].z, 0x5410), __byte_perm(u[j].x, u[j].z, 0x7632),
+                __byte_perm(u[j].y, u[j].w, 0x5410), __byte_perm(u[j].y, u[j].w, 0x7632));
+        }
+      }
+    };
+    stage_x(0, xs);
+    named_bar_sync(kI4ConsumerBar + G, kAll);
+    float ac[kI4XRItems][NT][4];
+#pragma unroll
+    for (int j = 0; j < kI4XRItems; ++j)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ac[j][nt][e] = 0.f;
+    bool dead = false;
+    const int box = warp >> 1, chunk = ((warp & 1) << 2) + t, swz = (chunk ^ g) << 4;
+    const int kloc = warp * kI4KIter + 32 * t;  // this lane's x column within the round
+    int q = 0;
+    for (int r = 0; r < a.rounds; ++r) {
+      // slice r + 1 goes to the buffer every group finished reading in round r - 1
+      if (r + 1 < a.rounds) stage_x(r + 1, xs + ((r + 1) & 1) * a.M * kXS);
+      const __half* xr = xs + (r & 1) * a.M * kXS;
+#pragma unroll
+      for (int j = 0; j < kI4XRItems; ++j) {
+        if (j >= my_items) break;
+        const int st = q % kSt;
+        if (!dead)
+          dead = !__all_sync(0xffffffffu, mbar_wait(&bars->full[st], (q / kSt) & 1, a.err));
+        const uint8_t* sbase = stages + st * kSB + box * (R * kI4BoxBytes);
+        const uint4 qa4 = *reinterpret_cast<const uint4*>(sbase + g * kI4BoxBytes + swz);
+        uint4 qb4 = make_uint4(0u, 0u, 0u, 0u);
+        if constexpr (R == kI4Rows)
+          qb4 = *reinterpret_cast<const uint4*>(sbase + (g + 8) * kI4BoxBytes + swz);
+        const uint16_t* sc = reinterpret_cast<const uint16_t*>(sstages + st * kScB);
+        const uint32_t s2a = splat16(sc[g * (kI4RoundK / 128) + warp]);
+        uint32_t s2b = 0u;
+        if constexpr (R == kI4Rows) s2b = splat16(sc[(g + 8) * (kI4RoundK / 128) + warp]);
+        fence_proxy_async_smem();  // generic reads before the next TMA write of the stage
+        mbar_arrive(&bars->empty[st]);
+        const uint32_t wa4[4] = {qa4.x, qa4.y, qa4.z, qa4.w};
+        const uint32_t wb4[4] = {qb4.x, qb4.y, qb4.z, qb4.w};
+#pragma unroll
+        for (int wd = 0; wd < 4; ++wd) {
+          uint32_t ba[4], bb[4] = {0u, 0u, 0u, 0u};
+          dequant_word_perm(wa4[wd], s2a, ba);
+          if constexpr (R == kI4Rows) dequant_word_perm(wb4[wd], s2b, bb);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const uint4 u = *reinterpret_cast<const uint4*>(xr + xo[nt] + kloc + 8 * wd);
+            mma_16816(ac[j][nt], ba[0], bb[0], ba[1], bb[1], u.x, u.y);
+            mma_16816(ac[j][nt], ba[2], bb[2], ba[3], bb[3], u.z, u.w);
+          }
+        }
+        ++q;
+      }
+      named_bar_sync(kI4ConsumerBar + G, kAll);
+    }
+    // items done: add the 8 warps' partial sums in warp order, store fp16
+#pragma unroll
+    for (int j = 0; j < kI4XRItems; ++j) {
+      if (j >= my_items) break;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (R == kI4Rows || e < 2)
+            red[warp][nt * 8 + 2 * t + (e & 1)][g + (e >> 1) * 8] = ac[j][nt][e];
+      named_bar_sync(group_bar, kI4Consumers * 32);
+      const int nbase = (slot + j * nslots) * R;
+      for (int i = tid; i < a.M * R; i += kI4Consumers * 32) {
+        const int m = i / R, rr = i - m * R, n = nbase + rr;
+        float sum = 0.f;
+#pragma unroll
+        for (int w = 0; w < kI4Consumers; ++w) sum += red[w][m][rr];
+        if (n < a.N) a.c[m * a.cs0 + n * a.cs1] = __float2half_rn(sum);
+      }
+      named_bar_sync(group_bar, kI4Consumers * 32);
+    }
+    return;
   }
 
   // scale of (row, k) for this lane; fetched one round ahead
@@ -476,30 +592,41 @@ constexpr size_t i4_smem_x_max() {
 
 // Opts each instance in to its largest shared-memory layout (once per device), sizes
 // the persistent grid with the occupancy calculator for this call's layout, launches.
-template <int NT, bool kSmemX, int G, int R>
+// Two x slices of up to NT*8 rows for the round-by-round staging.
+template <int NT>
+constexpr size_t i4_xr_bytes() {
+  return 2 * (size_t)NT * 8 * (kI4RoundK + 8) * 2;
+}
+
+template <int NT, bool kSmemX, int G, int R, bool kXR = false>
 static int launch_int4_gemm(cudaStream_t st, const CUtensorMap& tm, const CUtensorMap& tms,
                             const I4Args& a) {
   static DeviceOnce attr_once;
   {
     const cudaError_t e = attr_once.run([] {
-      const int max_smem =
-          (int)(i4_smem_base<NT, G, R>() + (kSmemX ? i4_smem_x_max<NT, G, R>() : 0));
-      return cudaFuncSetAttribute(int4_gemm_kernel<NT, kSmemX, G, R>,
+      const size_t x_max = kSmemX ? i4_smem_x_max<NT, G, R>() : kXR ? i4_xr_bytes<NT>() : 0;
+      const int max_smem = (int)(i4_smem_base<NT, G, R>() + x_max);
+      return cudaFuncSetAttribute(int4_gemm_kernel<NT, kSmemX, G, R, kXR>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
     });
     if (e != cudaSuccess) return cuda_fail(e, "fi_int4_gemm: cudaFuncSetAttribute");
   }
-  const size_t smem =
-      i4_smem_base<NT, G, R>() + (kSmemX ? (size_t)a.M * (size_t)a.xstride * 2 : 0);
+  const size_t smem = i4_smem_base<NT, G, R>() +
+                      (kSmemX ? (size_t)a.M * (size_t)a.xstride * 2
+                              : kXR ? 2 * (size_t)a.M * (kI4RoundK + 8) * 2 : 0);
   const int threads = G * kI4Threads;
   int nb = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, int4_gemm_kernel<NT, kSmemX, G, R>,
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, int4_gemm_kernel<NT, kSmemX, G, R, kXR>,
                                                     threads, smem) != cudaSuccess || nb < 1)
     nb = 1;
   const int items = (a.N + R - 1) / R;
+  // up to one CTA per item: with group-major slots, items beyond one per CTA go to the
+  // second group of different CTAs, so every SM gets work before any gets two items
   int grid = nb * sm_count();
-  if (grid > (items + G - 1) / G) grid = (items + G - 1) / G;
-  cudaError_t e = launch_pdl(int4_gemm_kernel<NT, kSmemX, G, R>, dim3((unsigned)grid),
+  if (grid > items) grid = items;
+  if (kXR && items > kI4XRItems * G * grid)
+    return fail(FI_ERR_UNSUPPORTED, "fi_int4_gemm: too many items for round-major staging");
+  cudaError_t e = launch_pdl(int4_gemm_kernel<NT, kSmemX, G, R, kXR>, dim3((unsigned)grid),
                              dim3(threads), smem, st, tm, tms, a);
   if (e != cudaSuccess) return cuda_fail(e, "fi_int4_gemm launch");
   return FI_OK;
@@ -516,6 +643,17 @@ static int launch_int4_gemm_nt(cudaStream_t st, const CUtensorMap& tm, const CUt
       return launch_int4_gemm<NT, true, 2, R>(st, tm, tms, a);
   }
   if (xbytes <= i4_smem_x_max<NT, 1, R>()) return launch_int4_gemm<NT, true, 1, R>(st, tm, tms, a);
+  if constexpr (NT == 2) {
+    // x by round: scales must come by TMA, every slot must hold at most kI4XRItems
+    // items (at least min(items, SMs) CTAs of two groups are launched), and there must
+    // be more items than SMs. Per call, batch 16, K = 8192 (x from global memory / by
+    // round): N = 3072 16.7 / 15.3 us, N = 5120 24.2 / 19.8; but N = 2368 (148 items)
+    // 9.6 / 11.9, where staging x every round costs more than the loads it saves.
+    const int64_t items = (a.N + R - 1) / R;
+    if (a.tma_scales && items > sm_count() && items <= (int64_t)kI4XRItems * 2 * sm_count() &&
+        i4_smem_base<NT, 2, R>() + i4_xr_bytes<NT>() + 1024 <= kI4SmemOptin)
+      return launch_int4_gemm<NT, false, 2, R, true>(st, tm, tms, a);
+  }
   return launch_int4_gemm<NT, false, 1, R>(st, tm, tms, a);
 }
 

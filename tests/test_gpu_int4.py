@@ -105,7 +105,11 @@ def test_llama_projection_shapes_vs_oracle(cuda_device, name, n, k, m):
 @pytest.mark.parametrize("n,k,gs,m", [(100, 256, 128, 3), (1000, 96, 32, 7), (130, 160, 32, 17),
                                       (8, 128, 128, 1), (257, 640, 64, 33), (4096, 4096, 128, 2),
                                       (8, 128, 128, 12), (100, 256, 128, 10), (130, 160, 32, 16),
-                                      (4112, 3072, 128, 9)])
+                                      (4112, 3072, 128, 9),
+                                      # x too large for shared memory at 9-16 tokens: staged
+                                      # round by round (group size 128), or read from
+                                      # global memory (group size 64)
+                                      (3000, 8192, 128, 11), (1000, 8192, 64, 16)])
 def test_ragged_shapes_and_group_sizes(cuda_device, n, k, gs, m):
     from fast_infer_b200.kernels.matmul import int4_matmul as gpu_mm
     w = _weights(n, k, 7 * n + k)
