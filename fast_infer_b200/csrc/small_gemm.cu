@@ -65,8 +65,9 @@ struct SgArgs {
   int64_t xs0, cs0, cs1, rs0, rs1;
 };
 
-struct SgBars {
-  uint64_t full[kSgStages], empty[kSgStages];
+constexpr int kSsDeepStages = 6;  // streamed variant, at most one CTA per SM (see below)
+struct SgBars {  // sized for the deepest ring (96 of the 256 bytes reserved)
+  uint64_t full[kSsDeepStages], empty[kSsDeepStages];
 };
 
 template <int NT>
@@ -352,7 +353,7 @@ __host__ __device__ constexpr size_t ss_smem_bytes() {
 }
 
 template <int NT, bool kFold, bool kRope, int kSsStages, bool kReduce = false>
-__global__ void __launch_bounds__(kSgThreads, kSsStages == 2 ? 3 : 2)
+__global__ void __launch_bounds__(kSgThreads, kSsStages == 2 ? 3 : kSsStages == 3 ? 2 : 1)
     small_gemm_stream_kernel(const __grid_constant__ CUtensorMap tm_w,
                              const __grid_constant__ CUtensorMap tm_x, const SsArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -669,10 +670,18 @@ static int launch_small_gemm_stream_s(cudaStream_t st, const CUtensorMap& tw,
 // Two 8-token tiles with more work items than two CTAs per SM can hold (but at most
 // three per SM): the 2-stage ring at three CTAs per SM avoids a second wave of items
 // (QKV 5120 x 3072 at 16 rows: 10.3 -> 8.5 us); otherwise the 3-stage ring is faster.
+// At most one item per SM (the per-rank QKV share of a KV-head-sharded stack: N = 640
+// at 8 GPUs, 1280 at 4): each CTA's item streams through a 6-stage ring, so more
+// weight bytes are in flight per SM than two or three CTAs would keep.
+#ifndef FI_SG_DEEP
+#define FI_SG_DEEP 1
+#endif
 template <int NT, bool kFold, bool kRope = false>
 static int launch_small_gemm_stream(cudaStream_t st, const CUtensorMap& tw, const CUtensorMap& tx,
                                     const SsArgs& a) {
   const int items = (a.N + kSgRows - 1) / kSgRows;
+  if (FI_SG_DEEP && items <= sm_count())
+    return launch_small_gemm_stream_s<NT, kFold, kRope, kSsDeepStages>(st, tw, tx, a);
   if (NT == 2 && items > 2 * sm_count() && items <= 3 * sm_count())
     return launch_small_gemm_stream_s<NT, kFold, kRope, 2>(st, tw, tx, a);
   return launch_small_gemm_stream_s<NT, kFold, kRope, 3>(st, tw, tx, a);
